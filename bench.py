@@ -1,0 +1,436 @@
+"""Benchmark of the SAM 3 ViT vision trunk on B200 (one process per GPU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--format f16|q8_0] [--images 64]
+    python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N ...
+    python bench.py --impl reference ...      # the reference's CPU trunk
+
+Workload (ours): the seeded SAM 3 trunk (random-init weights of the real
+architecture, GGUF in the requested format) on a batch of 64 synthetic
+1008x1008 images sharded by image across the N GPUs (64/N each), outputs
+gathered to rank 0 over NCCL.  One step = the whole batch through the trunk
+(+ the gather).  `value` = images/s of the whole job with inputs resident in
+HBM; `e2e` = the same through the public API with pinned host buffers
+(host->device images and device->host feature maps inside the timed region).
+Inputs (780 MB of images, 0.9 GB of weights, ~8 GB of activations per step)
+are far larger than the 126 MB L2, so no explicit flush is done.
+
+Rank 0 prints one JSON line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "ViT-trunk images/s @1008^2"
+FLOP_PER_IMAGE = 5.3986e12          # GEMMs 4609.6 GF + attention 782.8 GF + patch 6.24 GF
+GEMM_FLOP_PER_IMAGE_LAYER = 144.05e9  # 2*T*C*(3C + C + 2F), T=5184, C=1024, F=4736
+LAUNCHES_PER_TRUNK = 3 + 32 * 6 + 31  # im2col, patch GEMM, stem LN; 6 per block; 31 inter-block LNs
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d["bf16_tflops"], d.get("bf16_tflops_sustained"), d["hbm_gbs"], "measured"
+    return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples while the timed region runs."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}")
+    return world, rank, local
+
+
+# --------------------------------------------------------------- ours ---
+
+def run_ours(a):
+    import torch
+    import torch.distributed as dist
+
+    world, rank, local = dist_setup(a.gpus)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+
+    import sam3cpp_b200 as s3t
+    from sam3cpp_b200 import synthetic as syn
+
+    if a.images % world:
+        raise SystemExit("--images must be divisible by --gpus")
+    per = a.images // world
+
+    # model file: rank 0 writes it (cached), the others wait
+    if rank == 0:
+        path = syn.synthetic_gguf(a.format)
+    if world > 1:
+        dist.barrier()
+    path = syn.synthetic_gguf(a.format)
+    model = s3t.GgufModel(path, device=local)
+    trunk = s3t.VisionTrunk(model)
+
+    imgs_host = torch.from_numpy(syn.synthetic_images(per, start=rank * per)).pin_memory()
+    imgs = imgs_host.to(dev)
+    out = torch.empty((per, 1024, 72, 72), dtype=torch.float32, device=dev)
+    gathered = ([torch.empty_like(out) for _ in range(world)] if rank == 0 else None) if world > 1 else None
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        trunk.run_device(imgs.data_ptr(), per, out.data_ptr(), stream.cuda_stream)
+        if world > 1:
+            dist.gather(out, gathered, dst=0)
+
+    def timed(fn, k):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(k):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        ms = torch.tensor([e0.elapsed_time(e1)], device=dev)
+        if world > 1:
+            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        return float(ms.item())
+
+    for _ in range(a.warmup):
+        step()
+    trunk.sync(stream.cuda_stream)
+    with ClockSampler(local) as clk:
+        total_ms = timed(step, a.steps)
+    trunk.sync(stream.cuda_stream)
+    ms_step = total_ms / a.steps
+    value = a.images * a.steps / (total_ms / 1e3)
+
+    # e2e: public API with pinned host buffers (H2D + trunk + D2H per step)
+    out_host = torch.empty((per, 1024, 72, 72), dtype=torch.float32).pin_memory()
+
+    def e2e_step():
+        trunk.run_device(imgs_host.data_ptr(), per, out_host.data_ptr(), stream.cuda_stream,
+                         images_on_device=False, output_on_device=False)
+
+    for _ in range(max(1, a.warmup // 2)):
+        e2e_step()
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    e2e_ms = timed(e2e_step, a.steps)
+    e2e_wall = time.perf_counter() - t0
+    e2e_value = a.images * a.steps / (e2e_ms / 1e3)
+
+    # per-kernel live timing of the dominant kernels at this shape (outside the timed region)
+    kern = kernel_timings(torch, dev, stream, per)
+    extras = {}
+    if rank == 0 and world == 1 and not a.no_extras:
+        extras = config_extras(torch, dev, stream, trunk, syn, s3t)
+
+    if world > 1:
+        dist.barrier()
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
+    bf16_peak, bf16_sus, hbm_peak, peak_kind = measured_peaks()
+    gemm_ms = kern["gemm_ms_per_layer"]
+    gemm_flop = GEMM_FLOP_PER_IMAGE_LAYER * per
+    achieved = gemm_flop / (gemm_ms / 1e3) / 1e12
+    line = {
+        "metric": METRIC,
+        "value": round(value, 3),
+        "unit": "images/s",
+        "n_gpus": world,
+        "steps": a.steps,
+        "warmup": a.warmup,
+        "ms_per_step": round(ms_step, 3),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f16" if a.format != "q8_0" else "q8_0->f16",
+        "data": "synthetic (seeded random-init SAM 3 trunk weights, uniform[-1,1] images)",
+        "config": {
+            "workload": f"SAM 3 ViT trunk, {a.format.upper()} GGUF, {a.images} images 3x1008x1008 sharded by image "
+                        f"({per}/GPU), outputs gathered to rank 0",
+            "format": a.format, "global_batch": a.images, "per_gpu_batch": per, "tokens_per_image": 5184,
+            "layers": 32, "parallelism": f"image-sharded x{world}",
+            "l2_policy": "inputs and activations far larger than the 126 MB L2; no flush",
+        },
+        "roofline": {
+            "bound": "tensor",
+            "kernel": "gemm_tn_kernel (qkv+proj+fc1+fc2 of one block, M=%d)" % (per * 5184),
+            "achieved": round(achieved, 1), "peak": bf16_peak, "unit": "TFLOP/s",
+            "frac": round(achieved / bf16_peak, 4), "peak_kind": f"{peak_kind} bf16 burst",
+            "traffic": kern.get("traffic"),
+            "per_gemm_ms": kern["per_gemm_ms"],
+            "trunk_tensor_frac": round(FLOP_PER_IMAGE * value / world / 1e12 / bf16_peak, 4),
+        },
+        "e2e": {"value": round(e2e_value, 3), "unit": "images/s",
+                "h2d_bytes_per_step": int(imgs_host.numel() * 4 * world),
+                "d2h_bytes_per_step": int(out_host.numel() * 4 * world),
+                "wall_s": round(e2e_wall, 3)},
+        "clocks": clk.summary(),
+        "gpu_launches": LAUNCHES_PER_TRUNK * a.steps * world,
+        "attention": kern["attention"],
+        **extras,
+    }
+    if world == 1 and not a.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(a.format)
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def kernel_timings(torch, dev, stream, per):
+    """CUDA-event time of each GEMM of one block and of both attention kinds
+    at the bench's shape, launched through the C ABI on `stream`."""
+    import ctypes as C
+    from sam3cpp_b200 import lib, check
+    L = lib()
+    M = per * 5184
+    g = torch.Generator(device=dev).manual_seed(0)
+    x = torch.randn((M, 4736), generator=g, device=dev, dtype=torch.float16)
+    shapes = {"qkv": (3072, 1024), "proj": (1024, 1024), "fc1": (4736, 1024), "fc2": (1024, 4736)}
+    res = {}
+    y = torch.empty((M, 4736), device=dev, dtype=torch.float16)
+    for name, (N, K) in shapes.items():
+        w = torch.randn((N, K), generator=g, device=dev, dtype=torch.float16) * 0.02
+        b = torch.zeros(N, device=dev)
+        xs = x[:, :K].contiguous()
+        def launch():
+            check(L.s3t_gemm_f16(dev.index, C.c_void_p(xs.data_ptr()), C.c_void_p(w.data_ptr()),
+                                 C.c_void_p(b.data_ptr()), M, N, K, 1 if name == "fc1" else 0, 0,
+                                 C.c_void_p(y.data_ptr()), C.c_void_p(stream.cuda_stream)))
+        res[name] = _event_ms(torch, dev, stream, launch, 5, 10)
+        del xs
+    att = {}
+    for kind, (groups, Lk) in {"windowed": (9 * per, 576), "global": (per, 5184)}.items():
+        q, k, v = (torch.randn((groups * 16, Lk, 64), generator=g, device=dev, dtype=torch.float16) for _ in range(3))
+        o = torch.empty((per * 5184, 1024), device=dev, dtype=torch.float16)
+        def launch():
+            check(L.s3t_attention(dev.index, C.c_void_p(q.data_ptr()), C.c_void_p(k.data_ptr()),
+                                  C.c_void_p(v.data_ptr()), groups, Lk, 1 if kind == "windowed" else 0, 0,
+                                  C.c_void_p(o.data_ptr()), C.c_void_p(stream.cuda_stream)))
+        ms = _event_ms(torch, dev, stream, launch, 3, 10)
+        flop = 4.0 * groups * 16 * Lk * Lk * 64
+        att[kind] = {"ms": round(ms, 4), "tflops": round(flop / (ms / 1e3) / 1e12, 1)}
+        del q, k, v, o
+    check(L.s3t_device_status(dev.index))
+    return {"gemm_ms_per_layer": sum(res.values()), "per_gemm_ms": {k: round(v, 4) for k, v in res.items()},
+            "attention": att, "traffic": None}
+
+
+def _event_ms(torch, dev, stream, fn, warm, reps):
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    return e0.elapsed_time(e1) / reps
+
+
+def config_extras(torch, dev, stream, trunk, syn, s3t):
+    """Single-GPU extras: b=1 F16 p50 latency (device in -> device out) and
+    Q8_0 batch-8 throughput."""
+    img = torch.from_numpy(syn.synthetic_images(1)).to(dev)
+    out = torch.empty((1, 1024, 72, 72), device=dev)
+    lat = []
+    for i in range(110):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        trunk.run_device(img.data_ptr(), 1, out.data_ptr(), stream.cuda_stream)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        if i >= 10:
+            lat.append(e0.elapsed_time(e1))
+    res = {"latency_b1_p50_ms": round(statistics.median(lat), 3),
+           "latency_b1_p90_ms": round(sorted(lat)[int(0.9 * len(lat))], 3)}
+    try:
+        qm = s3t.GgufModel(syn.synthetic_gguf("q8_0"), device=dev.index)
+        qt = s3t.VisionTrunk(qm)
+        imgs = torch.from_numpy(syn.synthetic_images(8)).to(dev)
+        o8 = torch.empty((8, 1024, 72, 72), device=dev)
+        fn = lambda: qt.run_device(imgs.data_ptr(), 8, o8.data_ptr(), stream.cuda_stream)
+        ms = _event_ms(torch, dev, stream, fn, 3, 10)
+        qt.sync(stream.cuda_stream)
+        res["q8_0_b8_images_per_s"] = round(8 / (ms / 1e3), 2)
+        qm.close()
+    except Exception as e:  # reported, not fatal for the headline line
+        res["q8_0_b8_error"] = str(e)
+    return res
+
+
+def cpu_baseline(fmt):
+    """The reference's own CPU trunk (oracle/_ref: ggml CPU backend compiled
+    from the reference sources) on one image with all host threads."""
+    try:
+        from oracle.pyoracle import Reference
+        from sam3cpp_b200 import synthetic as syn
+        ref = Reference()
+        threads = os.cpu_count() or 1
+        _, sec = ref.trunk(syn.synthetic_gguf(fmt), syn.synthetic_image(0), threads)
+        return {"value": round(1.0 / sec, 5), "unit": "images/s", "cores": threads, "kind": "reference",
+                "sample": f"1 image, sam3::VisionTrunk::run ({fmt.upper()} GGUF), {sec:.1f} s, "
+                          f"{ref.path.name}"}
+    except Exception as e:
+        return {"value": None, "unit": "images/s", "cores": os.cpu_count(), "kind": "reference",
+                "sample": f"unavailable: {e}"}
+
+
+# ------------------------------------------------------------ reference ---
+
+def run_reference(a):
+    world, rank, _ = dist_setup(a.gpus)
+    if rank != 0:
+        return
+    from oracle.pyoracle import Reference
+    from sam3cpp_b200 import synthetic as syn
+    ref = Reference()
+    threads = os.cpu_count() or 1
+    path = str(syn.synthetic_gguf(a.format))
+    img = syn.synthetic_image(0)
+    import ctypes as C
+    h = ref.lib.ref_model_load(path.encode(), threads)
+    if not h:
+        print(json.dumps({"impl": "reference", "unavailable": ref.lib.ref_last_error().decode()}))
+        return
+    out = np.empty((1, 1024, 72, 72), np.float32)
+    sec = C.c_double()
+
+    def one():
+        rc = ref.lib.ref_model_run(h, img.ctypes.data, out.ctypes.data, C.byref(sec))
+        if rc != 0:
+            raise RuntimeError(ref.lib.ref_last_error().decode())
+        return sec.value
+
+    # One reference step is one image through sam3::VisionTrunk::run (tens of
+    # seconds on the host cores), so warm-up is capped at 1 and the timed
+    # steps at what fits ~150 s.
+    warm = min(a.warmup, 1)
+    t_first = None
+    for _ in range(warm):
+        t_first = one()
+    if t_first is None:
+        t_first = one()
+    k = max(1, min(a.steps, int(150.0 / max(t_first, 1e-3))))
+    t0 = time.perf_counter()
+    for _ in range(k):
+        one()
+    total = time.perf_counter() - t0
+    ref.lib.ref_model_free(h)
+    value = k / total
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 5), "unit": "images/s", "n_gpus": a.gpus,
+        "steps": k, "steps_requested": a.steps, "warmup": warm, "ms_per_step": round(total / k * 1e3, 1),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32 (ggml CPU)",
+        "data": "synthetic (seeded random-init SAM 3 trunk weights, uniform[-1,1] images)",
+        "config": {"workload": f"SAM 3 ViT trunk, {a.format.upper()} GGUF, 1 image per step (sample of the "
+                               f"{a.images}-image batch), ggml CPU backend, {threads} threads",
+                   "format": a.format},
+        "cpu_baseline": {"value": round(value, 5), "unit": "images/s", "cores": threads, "kind": "reference",
+                         "sample": f"{k} image(s) through sam3::VisionTrunk::run ({ref.path.name})"},
+        "e2e": {"value": round(value, 5), "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--format", default="f16", choices=["f16", "q8_0", "f32"])
+    ap.add_argument("--images", type=int, default=64)
+    ap.add_argument("--no-extras", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    a = ap.parse_args()
+    if a.warmup < 3 and a.impl == "ours":
+        print("note: fewer than 3 warm-up steps", file=sys.stderr)
+    if a.impl == "reference":
+        run_reference(a)
+    else:
+        run_ours(a)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,114 @@
+/* s3t — SAM 3 ViT vision trunk on NVIDIA B200 (sm_100a): the C ABI.
+ *
+ * Drop-in for the reference's vision-trunk entry point
+ *   sam3::VisionTrunk::run(image_nchw, shape_nchw)
+ *   (include/sam3/vision_trunk.h:15-26, src/vision_trunk.cpp:297-488),
+ * reading the same GGUF tensors (names resolved through the converter's
+ * <file>.tensor_map.json sidecar like src/gguf_model.cpp:28-47,190-204) in the
+ * same F32 / F16 / Q8_0 formats.
+ *
+ * Conventions follow the reference's C API (include/sam3/c_api.h,
+ * src/c_api.cpp:19-23): functions return 0 on success and -1 on failure with
+ * a thread-local message from s3t_last_error(); nothing throws across the ABI;
+ * buffers passed in are borrowed, never freed.  One context is bound to one
+ * GPU and is not safe for concurrent calls (like the reference's
+ * VisionTrunk::run, which shares the backend's work buffer).
+ */
+#ifndef S3T_H
+#define S3T_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ggml type codes of the weight formats (ggml/include/ggml.h GGML_TYPE_*). */
+enum { S3T_TYPE_F32 = 0, S3T_TYPE_F16 = 1, S3T_TYPE_Q8_0 = 8 };
+
+/* s3t_trunk_run flags: where the image and output buffers live. */
+enum {
+    S3T_IMAGES_ON_DEVICE = 1, /* images_nchw is a device pointer on the context's GPU */
+    S3T_OUTPUT_ON_DEVICE = 2, /* out_nchw is a device pointer on the context's GPU */
+};
+
+typedef struct s3t_ctx s3t_ctx;
+
+/* Create a context on CUDA device `device`.  Replaces GgufModel::load's
+ * backend selection (src/gguf_model.cpp:107-120) for the trunk.  NULL on error. */
+s3t_ctx *s3t_create(int device);
+void s3t_destroy(s3t_ctx *ctx);
+const char *s3t_last_error(void);
+
+/* Stage one trunk tensor (host bytes, ggml layout: ne[0] fastest).  `name`
+ * is the original (unhashed) tensor name, e.g.
+ * "backbone.vision_backbone.trunk.blocks.3.attn.qkv.weight".  Replaces the
+ * per-tensor ggml_backend_tensor_set of src/gguf_model.cpp:150-153. */
+int s3t_set_weight(s3t_ctx *ctx, const char *name, int ggml_type, const int64_t ne[4], const void *host_bytes,
+                   size_t nbytes);
+
+/* Read every trunk tensor of a GGUF file (GgufModel::load,
+ * src/gguf_model.cpp:83-168).  tensor_map_path may be NULL, meaning
+ * "<gguf_path>.tensor_map.json" if that file exists. */
+int s3t_load_gguf(s3t_ctx *ctx, const char *gguf_path, const char *tensor_map_path);
+
+/* Validate shapes/types of the staged tensors, upload them and convert them
+ * to the GEMM operand format (Q8_0 / F32 -> fp16 on the device, patch-embed
+ * repacked).  Must be called once before the first run. */
+int s3t_finalize_weights(s3t_ctx *ctx);
+
+/* Number of transformer blocks found in the weights (32 for SAM 3). */
+int s3t_num_layers(const s3t_ctx *ctx);
+
+/* The trunk: images [batch][3][1008][1008] fp32 -> out [batch][1024][72][72]
+ * fp32, both NCHW (VisionTrunk::run, src/vision_trunk.cpp:297-488, with the
+ * batch of 1 generalised to `batch` independent images).  stream is a
+ * cudaStream_t or NULL for the context's own stream.  With host buffers the
+ * call returns after the output is in host memory; with both buffers on the
+ * device it returns after enqueueing (check with s3t_sync). */
+int s3t_trunk_run(s3t_ctx *ctx, const float *images_nchw, int batch, float *out_nchw, int flags, void *stream);
+
+/* Same, stopping after the first n_layers blocks (0 = patch embed + pos +
+ * ln_pre only).  Mirrors the per-stage dumps of the reference's
+ * tools/export_vision_trunk_reference.py (.stem/.ln_pre/.layer_NN). */
+int s3t_trunk_run_layers(s3t_ctx *ctx, const float *images_nchw, int batch, int n_layers, float *out_nchw, int flags,
+                         void *stream);
+
+/* Wait for the context's queued work and report any device-side error. */
+int s3t_sync(s3t_ctx *ctx, void *stream);
+
+/* --- op-level entry points (parity tests, microbenchmarks) --------------- */
+
+/* Dequantize GGUF weight bytes on the device to fp32: F16 and Q8_0
+ * (dequantize_row_q8_0, ggml/src/ggml-quants.c:436-450).  Device pointers. */
+int s3t_dequantize(int ggml_type, const void *src_dev, int64_t n, float *dst_dev, void *stream);
+
+/* y16[M][N] = fp16(act(x16[M][K] * w16[N][K]^T + bias)) — the trunk's GEMM
+ * (ggml_mul_mat + bias, src/vision_trunk.cpp:50-62).  act: 0 none, 1 GELU-erf.
+ * q8: apply the Q8_0 activation rounding to the output.  Device pointers. */
+int s3t_gemm_f16(int device, const void *x16, const void *w16, const float *bias, int M, int N, int K, int act,
+                 int q8, void *y16, void *stream);
+
+/* Flash attention on grouped, already-rotated q/k/v [groups*16][L][64]
+ * (fp16 or bf16), output token-major [images*5184][1024] in natural token
+ * order (windowed: 9 groups per image).  Device pointers. */
+int s3t_attention(int device, const void *q, const void *k, const void *v, int groups, int L, int windowed, int bf16,
+                  void *out, void *stream);
+
+/* Axial RoPE in place on grouped q or k (layout as above). */
+int s3t_rope(int device, void *x, int groups, int L, int windowed, int bf16, void *stream);
+
+/* LayerNorm over 1024 columns (eps 1e-5), fp32 in -> fp16 out (q8: Q8_0
+ * activation rounding of the output).  Device pointers. */
+int s3t_layernorm(int device, const float *x, int rows, const float *gamma, const float *beta, void *y16, int q8,
+                  void *stream);
+
+/* Synchronize `device` and report (then clear) the device status word that
+ * the op-level entry points write when a bounded in-kernel wait times out. */
+int s3t_device_status(int device);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

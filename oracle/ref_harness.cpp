@@ -1,0 +1,227 @@
+// Test-infrastructure harness around the reference's own CPU code.
+//
+// Compiled by oracle/Makefile together with the reference's ggml sources and
+// src/vision_trunk.cpp + src/gguf_model.cpp, straight from where they lie in
+// the reference tree, into oracle/_ref/libsam3ref_*.so.  It is only ever used
+// as a checker (pinning the C restatement in s3t_oracle.c) and as the timed
+// CPU baseline; nothing in the product links it.
+//
+// Every entry point runs one small ggml graph on the ggml CPU backend, in the
+// style of ggml/tests/test-backend-ops.cpp, or the reference trunk itself.
+// All functions return 0 on success and -1 on failure.
+
+#include "ggml.h"
+#include "ggml-cpu.h"
+#include "ggml-backend.h"
+#include "sam3/gguf_model.h"
+#include "sam3/vision_trunk.h"
+
+#include <chrono>
+#include <cstdint>
+#include <cstring>
+#include <exception>
+#include <string>
+#include <vector>
+
+namespace {
+
+thread_local std::string g_err;
+
+struct Ctx {
+    ggml_context * ctx = nullptr;
+    explicit Ctx(size_t bytes) {
+        ggml_init_params p{bytes, nullptr, false};
+        ctx = ggml_init(p);
+    }
+    ~Ctx() { if (ctx) ggml_free(ctx); }
+};
+
+int compute(ggml_context * ctx, ggml_tensor * out, int n_threads) {
+    ggml_cgraph * gf = ggml_new_graph_custom(ctx, 4096, false);
+    ggml_build_forward_expand(gf, out);
+    return ggml_graph_compute_with_ctx(ctx, gf, n_threads) == GGML_STATUS_SUCCESS ? 0 : -1;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char * ref_last_error(void) { return g_err.c_str(); }
+
+// sam3::VisionTrunk::run (src/vision_trunk.cpp:297) on the ggml CPU backend.
+// image: [1,3,1008,1008] fp32; out: [1,1024,72,72] fp32.  *seconds receives the
+// wall time of run() alone (model load excluded).
+int ref_trunk_run(const char * gguf_path, const float * image, float * out,
+                  int n_threads, double * seconds) {
+    try {
+        sam3::GgufModel model;
+        if (!model.load(gguf_path, /*prefer_gpu=*/false)) {
+            g_err = "failed to load model";
+            return -1;
+        }
+        if (n_threads > 0) ggml_backend_cpu_set_n_threads(model.backend(), n_threads);
+        std::vector<float> img(image, image + 3ull * 1008 * 1008);
+        sam3::VisionTrunk trunk(model);
+        auto t0 = std::chrono::steady_clock::now();
+        sam3::VisionTrunkOutput r = trunk.run(img, {1, 3, 1008, 1008});
+        auto t1 = std::chrono::steady_clock::now();
+        if (seconds) *seconds = std::chrono::duration<double>(t1 - t0).count();
+        std::memcpy(out, r.trunk_nchw.data(), r.trunk_nchw.size() * sizeof(float));
+        return 0;
+    } catch (const std::exception & e) {
+        g_err = e.what();
+        return -1;
+    }
+}
+
+// Load once, run many: keeps the GgufModel alive so the CPU baseline can time
+// repeated VisionTrunk::run calls without the load.
+void * ref_model_load(const char * gguf_path, int n_threads) {
+    auto * m = new sam3::GgufModel();
+    if (!m->load(gguf_path, false)) { delete m; g_err = "failed to load model"; return nullptr; }
+    if (n_threads > 0) ggml_backend_cpu_set_n_threads(m->backend(), n_threads);
+    return m;
+}
+
+int ref_model_run(void * handle, const float * image, float * out, double * seconds) {
+    try {
+        auto * m = static_cast<sam3::GgufModel *>(handle);
+        std::vector<float> img(image, image + 3ull * 1008 * 1008);
+        sam3::VisionTrunk trunk(*m);
+        auto t0 = std::chrono::steady_clock::now();
+        sam3::VisionTrunkOutput r = trunk.run(img, {1, 3, 1008, 1008});
+        auto t1 = std::chrono::steady_clock::now();
+        if (seconds) *seconds = std::chrono::duration<double>(t1 - t0).count();
+        if (out) std::memcpy(out, r.trunk_nchw.data(), r.trunk_nchw.size() * sizeof(float));
+        return 0;
+    } catch (const std::exception & e) {
+        g_err = e.what();
+        return -1;
+    }
+}
+
+void ref_model_free(void * handle) { delete static_cast<sam3::GgufModel *>(handle); }
+
+// y[M][N] = ggml_mul_mat(W, x): W has ggml type wtype (0=F32, 1=F16, 8=Q8_0)
+// and ne = [K, N] (row n holds output channel n, K contiguous); x is f32 [M][K].
+int ref_mul_mat(int wtype, const void * w, int64_t N, int64_t K, const float * x,
+                int64_t M, float * y, int n_threads) {
+    const ggml_type t = (ggml_type) wtype;
+    const size_t wbytes = ggml_row_size(t, K) * N;
+    Ctx c(wbytes + (size_t) (M * K + M * N) * 4 * 2 + 64 * 1024 * 1024);
+    ggml_tensor * tw = ggml_new_tensor_2d(c.ctx, t, K, N);
+    ggml_tensor * tx = ggml_new_tensor_2d(c.ctx, GGML_TYPE_F32, K, M);
+    std::memcpy(tw->data, w, wbytes);
+    std::memcpy(tx->data, x, (size_t) M * K * 4);
+    ggml_tensor * ty = ggml_mul_mat(c.ctx, tw, tx);
+    if (compute(c.ctx, ty, n_threads)) return -1;
+    std::memcpy(y, ty->data, (size_t) M * N * 4);
+    return 0;
+}
+
+// ggml_norm (eps) over rows of x [rows][cols]; no affine part.
+int ref_norm(const float * x, int64_t rows, int64_t cols, float eps, float * y) {
+    Ctx c((size_t) rows * cols * 4 * 3 + 16 * 1024 * 1024);
+    ggml_tensor * tx = ggml_new_tensor_2d(c.ctx, GGML_TYPE_F32, cols, rows);
+    std::memcpy(tx->data, x, (size_t) rows * cols * 4);
+    ggml_tensor * ty = ggml_norm(c.ctx, tx, eps);
+    if (compute(c.ctx, ty, 4)) return -1;
+    std::memcpy(y, ty->data, (size_t) rows * cols * 4);
+    return 0;
+}
+
+// The axial RoPE of src/vision_trunk.cpp:145-205 built from the same ggml ops:
+// x is [tokens][heads][64] f32; dims 0..31 rotate with pos_x, 32..63 with pos_y.
+int ref_rope_axial(const float * x, int64_t tokens, int64_t heads, const int32_t * pos_x,
+                   const int32_t * pos_y, float freq_scale, float * y) {
+    const size_t n = (size_t) tokens * heads * 64;
+    Ctx c(n * 4 * 8 + 16 * 1024 * 1024);
+    ggml_tensor * tx = ggml_new_tensor_4d(c.ctx, GGML_TYPE_F32, 64, heads, tokens, 1);
+    ggml_tensor * px = ggml_new_tensor_1d(c.ctx, GGML_TYPE_I32, tokens);
+    ggml_tensor * py = ggml_new_tensor_1d(c.ctx, GGML_TYPE_I32, tokens);
+    std::memcpy(tx->data, x, n * 4);
+    std::memcpy(px->data, pos_x, tokens * 4);
+    std::memcpy(py->data, pos_y, tokens * 4);
+    ggml_tensor * first = ggml_view_4d(c.ctx, tx, 32, heads, tokens, 1, tx->nb[1], tx->nb[2], tx->nb[3], 0);
+    ggml_tensor * second = ggml_view_4d(c.ctx, tx, 32, heads, tokens, 1, tx->nb[1], tx->nb[2], tx->nb[3], 32 * 4);
+    first = ggml_rope_ext(c.ctx, first, px, nullptr, 32, 0, 32768, 10000.0f, freq_scale, 0.0f, 1.0f, 0.0f, 0.0f);
+    second = ggml_rope_ext(c.ctx, second, py, nullptr, 32, 0, 32768, 10000.0f, freq_scale, 0.0f, 1.0f, 0.0f, 0.0f);
+    ggml_tensor * ty = ggml_concat(c.ctx, first, second, 0);
+    if (compute(c.ctx, ty, 4)) return -1;
+    std::memcpy(y, ty->data, n * 4);
+    return 0;
+}
+
+// ggml_flash_attn_ext with no mask, prec F32, as src/vision_trunk.cpp:207-228.
+// q: [nq][heads][d], k/v: [nk][heads][d] f32; out: [nq][heads][d] f32.
+int ref_flash_attn(const float * q, const float * k, const float * v, int64_t nq, int64_t nk,
+                   int64_t heads, int64_t d, float scale, float * out, int n_threads) {
+    const size_t bytes = (size_t) (2 * nq + 2 * nk) * heads * d * 4;
+    Ctx c(bytes * 2 + (size_t) nq * nk * 8 + 64 * 1024 * 1024);
+    ggml_tensor * tq = ggml_new_tensor_4d(c.ctx, GGML_TYPE_F32, d, heads, nq, 1);
+    ggml_tensor * tk = ggml_new_tensor_4d(c.ctx, GGML_TYPE_F32, d, heads, nk, 1);
+    ggml_tensor * tv = ggml_new_tensor_4d(c.ctx, GGML_TYPE_F32, d, heads, nk, 1);
+    std::memcpy(tq->data, q, (size_t) nq * heads * d * 4);
+    std::memcpy(tk->data, k, (size_t) nk * heads * d * 4);
+    std::memcpy(tv->data, v, (size_t) nk * heads * d * 4);
+    ggml_tensor * r = ggml_flash_attn_ext(c.ctx, ggml_permute(c.ctx, tq, 0, 2, 1, 3),
+                                          ggml_permute(c.ctx, tk, 0, 2, 1, 3),
+                                          ggml_permute(c.ctx, tv, 0, 2, 1, 3), nullptr, scale, 0.0f, 0.0f);
+    ggml_flash_attn_ext_set_prec(r, GGML_PREC_F32);
+    if (compute(c.ctx, r, n_threads)) return -1;
+    std::memcpy(out, r->data, (size_t) nq * heads * d * 4);
+    return 0;
+}
+
+int ref_gelu_erf(const float * x, int64_t n, float * y) {
+    Ctx c((size_t) n * 4 * 3 + 16 * 1024 * 1024);
+    ggml_tensor * tx = ggml_new_tensor_1d(c.ctx, GGML_TYPE_F32, n);
+    std::memcpy(tx->data, x, n * 4);
+    ggml_tensor * ty = ggml_gelu_erf(c.ctx, tx);
+    if (compute(c.ctx, ty, 1)) return -1;
+    std::memcpy(y, ty->data, n * 4);
+    return 0;
+}
+
+// The activation quantizer ggml's CPU mul_mat applies before a Q8_0 dot
+// (type_traits_cpu[Q8_0].from_float, ggml-cpu/arch/x86/quants.c).
+int ref_quantize_q8_0_act(const float * x, int64_t n, void * blocks) {
+    ggml_cpu_init();
+    const auto * tr = ggml_get_type_traits_cpu(GGML_TYPE_Q8_0);
+    tr->from_float(x, blocks, n);
+    return 0;
+}
+
+// The file-format dequantizers (ggml type_traits.to_float): F16 and Q8_0.
+int ref_to_float(int type, const void * src, int64_t n, float * y) {
+    const auto * tr = ggml_get_type_traits((ggml_type) type);
+    if (!tr->to_float) { g_err = "no to_float"; return -1; }
+    tr->to_float(src, y, n);
+    return 0;
+}
+
+int ref_fp32_to_fp16(const float * x, int64_t n, uint16_t * y) {
+    ggml_fp32_to_fp16_row(x, (ggml_fp16_t *) y, n);
+    return 0;
+}
+
+// Patch embed + token-major permute as src/vision_trunk.cpp:284-291,364-368.
+// w: GGUF patch_embed.proj.weight bytes, ne = [3,14,14,1024] of type wtype;
+// image [3][1008][1008] f32; out [5184][1024] f32 (token-major, x fastest).
+int ref_patch_embed(int wtype, const void * w, const float * image, float * out, int n_threads) {
+    const ggml_type t = (ggml_type) wtype;
+    const int64_t wn = 3 * 14 * 14 * 1024;
+    Ctx c((size_t) 1024 * 1024 * 1024);
+    ggml_tensor * tw = ggml_new_tensor_4d(c.ctx, t, 3, 14, 14, 1024);
+    ggml_tensor * ti = ggml_new_tensor_4d(c.ctx, GGML_TYPE_F32, 1008, 1008, 3, 1);
+    std::memcpy(tw->data, w, ggml_row_size(t, wn));
+    std::memcpy(ti->data, image, (size_t) 3 * 1008 * 1008 * 4);
+    ggml_tensor * wg = ggml_cont(c.ctx, ggml_permute(c.ctx, tw, 2, 0, 1, 3));
+    ggml_tensor * r = ggml_conv_2d(c.ctx, wg, ti, 14, 14, 0, 0, 1, 1);
+    r = ggml_cont(c.ctx, ggml_permute(c.ctx, r, 1, 2, 0, 3));
+    if (compute(c.ctx, r, n_threads)) return -1;
+    std::memcpy(out, r->data, (size_t) 5184 * 1024 * 4);
+    return 0;
+}
+
+}  // extern "C"

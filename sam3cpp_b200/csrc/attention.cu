@@ -1,0 +1,317 @@
+// Flash attention for the trunk (d = 64, 16 heads, no mask), tcgen05 based.
+//
+// Semantics: ggml_flash_attn_ext with scale 1/8 and F32 precision as used by
+// apply_attention (src/vision_trunk.cpp:207-228): out = softmax(q k^T / 8) v.
+// Windowed layers attend within each 24x24 window (L = 576 keys), global
+// layers over the 72x72 grid (L = 5184).  RoPE was already applied by the QKV
+// GEMM epilogue; window partition/unpartition (:235-282) is pure addressing:
+// q/k/v arrive grouped per (window, head) and the output is written back to
+// natural token order, so no permute copy exists.
+//
+// One CTA = one 128-query tile of one (group, head).  Roles (192 threads):
+// warp 0 TMA producer (Q once, K/V 64-key blocks into a 3-deep ring), warp 1
+// TMEM owner + UMMA issuer, warps 2..5 softmax (one query row per thread).
+//   S = Q K^T   : UMMA M=128 N=64 K=64, accumulator in TMEM cols [0,64)
+//   P = exp2(S*scale*log2e - m) written as fp16/bf16 into a swizzled smem tile
+//   O += P V    : UMMA M=128 N=64 K=64 (V MN-major), accumulator in TMEM [64,128)
+// S_{j+1} is issued as soon as the softmax warps have read S_j, so the tensor
+// core overlaps the exponentials; O is rescaled in TMEM when the row max grows.
+// L is a multiple of 64 for both layer kinds, so keys are never masked; query
+// rows past L (last tile) are computed on zero-filled Q rows and not stored.
+#include "kernels.h"
+#include "ptx.cuh"
+
+namespace s3t {
+
+namespace {
+
+constexpr int kBQ = 128, kBKV = 64, kD = 64, kKVStages = 3;
+constexpr uint32_t kQBytes = kBQ * kD * 2;      // 16 KB
+constexpr uint32_t kKVBytes = kBKV * kD * 2;    // 8 KB (each of K, V)
+constexpr uint32_t kPBytes = kBQ * kBKV * 2;    // 16 KB
+constexpr size_t kAttnSmem = kQBytes + 2 * kKVStages * kKVBytes + kPBytes + 1024 + 256;
+constexpr uint32_t kAttnTmemCols = 128;
+
+template <int BF16>
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+    if constexpr (BF16) return pack_bf162(a, b);
+    else return pack_half2(a, b);
+}
+
+template <int BF16>
+__global__ void __launch_bounds__(192, 2)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const AttnArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sQ = smem;
+    uint8_t* sK = sQ + kQBytes;
+    uint8_t* sV = sK + kKVStages * kKVBytes;
+    uint8_t* sP = sV + kKVStages * kKVBytes;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sP + kPBytes);
+    uint64_t* q_full = bars;
+    uint64_t* kv_full = bars + 1;
+    uint64_t* kv_empty = kv_full + kKVStages;
+    uint64_t* s_full = kv_empty + kKVStages;
+    uint64_t* s_free = s_full + 1;
+    uint64_t* p_full = s_free + 1;
+    uint64_t* o_done = p_full + 1;
+    uint64_t* drain = o_done + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int qt = blockIdx.x, head = blockIdx.y, grp = blockIdx.z;
+    const int bh = grp * kHeads + head;
+    const int nkv = a.L / kBKV;
+
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 1);
+        for (int s = 0; s < kKVStages; ++s) {
+            mbar_init(kv_full + s, 1);
+            mbar_init(kv_empty + s, 1);
+        }
+        mbar_init(s_full, 1);
+        mbar_init(s_free, 4);
+        mbar_init(p_full, 4);
+        mbar_init(o_done, 1);
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmQ);
+        tma_prefetch_desc(&tmK);
+        tma_prefetch_desc(&tmV);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, kAttnTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t tS = tmem, tO = tmem + 64;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            uint32_t armed = 0, armed_parity = 0;
+            bool ok = true;
+            mbar_arrive_expect_tx(q_full, kQBytes);
+            tma_load_3d(sQ, &tmQ, q_full, 0, qt * kBQ, bh);
+            for (int j = 0; j < nkv; ++j) {
+                const int s = j % kKVStages;
+                const uint32_t ph = (j / kKVStages) & 1;
+                if (!mbar_wait(kv_empty + s, ph ^ 1, a.status, kErrTimeoutProducer, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                mbar_arrive_expect_tx(kv_full + s, 2 * kKVBytes);
+                tma_load_3d(sK + s * kKVBytes, &tmK, kv_full + s, 0, j * kBKV, bh);
+                tma_load_3d(sV + s * kKVBytes, &tmV, kv_full + s, 0, j * kBKV, bh);
+                armed |= 1u << s;
+                armed_parity = (armed_parity & ~(1u << s)) | (ph << s);
+            }
+            if (!ok) {
+                mbar_wait(q_full, 0, a.status, kErrTimeoutDrain, nullptr);
+                for (int i = 0; i < kKVStages; ++i)
+                    if (armed & (1u << i))
+                        mbar_wait(kv_full + i, (armed_parity >> i) & 1u, a.status, kErrTimeoutDrain, nullptr);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idS = umma_idesc_f16(kBQ, kBKV, BF16, 0);
+            constexpr uint32_t idO = umma_idesc_f16(kBQ, kD, BF16, 1);
+            const uint32_t q0 = smem_u32(sQ), p0 = smem_u32(sP);
+            bool ok = true, issued = false;
+            auto issue_s = [&](int j) -> bool {
+                const int s = j % kKVStages;
+                if (!mbar_wait(kv_full + s, (j / kKVStages) & 1, a.status, kErrTimeoutMma, abort_flag)) return false;
+                if (j > 0 && !mbar_wait(s_free, (j - 1) & 1, a.status, kErrTimeoutMma, abort_flag)) return false;
+                tc_fence_after();
+                const uint32_t k0 = smem_u32(sK + s * kKVBytes);
+#pragma unroll
+                for (int k = 0; k < kD / 16; ++k)
+                    umma_f16_ss(tS, umma_desc_sw128(q0 + k * 32, 16, 1024), umma_desc_sw128(k0 + k * 32, 16, 1024), idS,
+                                k != 0);
+                umma_commit(s_full);
+                issued = true;
+                return true;
+            };
+            if (!mbar_wait(q_full, 0, a.status, kErrTimeoutMma, abort_flag)) ok = false;
+            if (ok) ok = issue_s(0);
+            for (int j = 0; ok && j < nkv; ++j) {
+                if (j + 1 < nkv && !issue_s(j + 1)) {
+                    ok = false;
+                    break;
+                }
+                if (!mbar_wait(p_full, j & 1, a.status, kErrTimeoutMma, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const int s = j % kKVStages;
+                const uint32_t v0 = smem_u32(sV + s * kKVBytes);
+#pragma unroll
+                for (int k = 0; k < kBKV / 16; ++k)
+                    umma_f16_ss(tO, umma_desc_sw128(p0 + k * 32, 16, 1024),
+                                umma_desc_sw128(v0 + k * 16 * 128, kKVBytes, 1024), idO, (j | k) != 0);
+                umma_commit(kv_empty + s);
+                umma_commit(o_done);
+            }
+            if (!ok && issued) {
+                umma_commit(drain);
+                mbar_wait(drain, 0, a.status, kErrTimeoutDrain, nullptr);
+            }
+        }
+    } else {
+        const int quarter = warp & 3;
+        const int row = quarter * 32 + lane;
+        const uint32_t lane_off = uint32_t(quarter * 32) << 16;
+        const float sl2 = a.scale_log2;
+        float m_run = -INFINITY, l_run = 0.f;
+        bool ok = true;
+        for (int j = 0; j < nkv; ++j) {
+            if (!mbar_wait(s_full, j & 1, a.status, kErrTimeoutEpilogue, abort_flag)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            uint32_t r0[32], r1[32];
+            tmem_ld32(tS + lane_off, r0);
+            tmem_ld32(tS + lane_off + 32, r1);
+            tmem_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(s_free);
+
+            float mx = -INFINITY;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) mx = fmaxf(mx, fmaxf(__uint_as_float(r0[i]), __uint_as_float(r1[i])));
+            const float m_new = fmaxf(m_run, mx * sl2);
+            const float alpha = ex2_approx(m_run - m_new);
+            float sum = 0.f;
+            uint32_t pk[32];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const float e0 = ex2_approx(fmaf(__uint_as_float(r0[2 * i]), sl2, -m_new));
+                const float e1 = ex2_approx(fmaf(__uint_as_float(r0[2 * i + 1]), sl2, -m_new));
+                const float f0 = ex2_approx(fmaf(__uint_as_float(r1[2 * i]), sl2, -m_new));
+                const float f1 = ex2_approx(fmaf(__uint_as_float(r1[2 * i + 1]), sl2, -m_new));
+                sum += (e0 + e1) + (f0 + f1);
+                pk[i] = pack2<BF16>(e0, e1);
+                pk[16 + i] = pack2<BF16>(f0, f1);
+            }
+            l_run = l_run * alpha + sum;
+
+            if (j > 0) {
+                if (!mbar_wait(o_done, (j - 1) & 1, a.status, kErrTimeoutEpilogue, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                if (__any_sync(0xffffffffu, alpha < 1.0f)) {
+                    uint32_t o0[32], o1[32];
+                    tmem_ld32(tO + lane_off, o0);
+                    tmem_ld32(tO + lane_off + 32, o1);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        o0[i] = __float_as_uint(__uint_as_float(o0[i]) * alpha);
+                        o1[i] = __float_as_uint(__uint_as_float(o1[i]) * alpha);
+                    }
+                    tmem_st32(tO + lane_off, o0);
+                    tmem_st32(tO + lane_off + 32, o1);
+                    tmem_wait_st();
+                }
+            }
+            // P row -> 128-byte swizzled smem row (16-byte chunk c at c ^ (row & 7)).
+            uint8_t* prow = sP + row * 128;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                uint4 u = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+                *reinterpret_cast<uint4*>(prow + ((c ^ (row & 7)) << 4)) = u;
+            }
+            fence_proxy_async_smem();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(p_full);
+            m_run = m_new;
+        }
+        if (ok && mbar_wait(o_done, (nkv - 1) & 1, a.status, kErrTimeoutEpilogue, abort_flag)) {
+            tc_fence_after();
+            uint32_t o0[32], o1[32];
+            tmem_ld32(tO + lane_off, o0);
+            tmem_ld32(tO + lane_off + 32, o1);
+            tmem_wait_ld();
+            const int qi = qt * kBQ + row;
+            if (qi < a.L) {
+                const float inv = 1.0f / l_run;
+                float v[2][32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    v[0][i] = __uint_as_float(o0[i]) * inv;
+                    v[1][i] = __uint_as_float(o1[i]) * inv;
+                }
+                if (a.q8) {
+                    q8_0_fake_quant32(v[0]);
+                    q8_0_fake_quant32(v[1]);
+                }
+                int img, tok;
+                if (a.windowed) {
+                    img = grp / 9;
+                    const int w = grp - img * 9, wy = w / 3, wx = w - wy * 3;
+                    const int ly = qi / kWindow, lx = qi - ly * kWindow;
+                    tok = (wy * kWindow + ly) * kGrid + wx * kWindow + lx;
+                } else {
+                    img = grp;
+                    tok = qi;
+                }
+                uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.out) +
+                                                      (int64_t(img) * kTokens + tok) * kDim + head * kD);
+#pragma unroll
+                for (int h = 0; h < 2; ++h)
+#pragma unroll
+                    for (int c = 0; c < 4; ++c)
+                        dst[h * 4 + c] = make_uint4(pack2<BF16>(v[h][8 * c], v[h][8 * c + 1]),
+                                                    pack2<BF16>(v[h][8 * c + 2], v[h][8 * c + 3]),
+                                                    pack2<BF16>(v[h][8 * c + 4], v[h][8 * c + 5]),
+                                                    pack2<BF16>(v[h][8 * c + 6], v[h][8 * c + 7]));
+            }
+        }
+    }
+
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kAttnTmemCols);
+    }
+}
+
+}  // namespace
+
+cudaError_t attention_prepare() {
+    cudaError_t e = cudaFuncSetAttribute(attn_fwd_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kAttnSmem));
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(attn_fwd_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kAttnSmem));
+}
+
+cudaError_t launch_attention(const AttnArgs& a, cudaStream_t stream) {
+    if (a.L % kBKV != 0 || a.groups <= 0) return cudaErrorInvalidValue;
+    const CUtensorMapDataType dt = a.bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const uint64_t zdim = uint64_t(a.groups) * kHeads;
+    CUtensorMap tq, tk, tv;
+    if (!make_tmap_3d(&tq, a.q, dt, 2, kD, a.L, zdim, kD, kBQ)) return cudaErrorInvalidValue;
+    if (!make_tmap_3d(&tk, a.k, dt, 2, kD, a.L, zdim, kD, kBKV)) return cudaErrorInvalidValue;
+    if (!make_tmap_3d(&tv, a.v, dt, 2, kD, a.L, zdim, kD, kBKV)) return cudaErrorInvalidValue;
+    dim3 grid((a.L + kBQ - 1) / kBQ, kHeads, a.groups);
+    if (a.bf16)
+        attn_fwd_kernel<1><<<grid, 192, kAttnSmem, stream>>>(tq, tk, tv, a);
+    else
+        attn_fwd_kernel<0><<<grid, 192, kAttnSmem, stream>>>(tq, tk, tv, a);
+    return cudaGetLastError();
+}
+
+}  // namespace s3t

@@ -1,0 +1,399 @@
+// Persistent, warp-specialized tcgen05 GEMM for the trunk's linears:
+//   C[M,N] = A[M,K] * B[N,K]^T,  A = activations fp16, B = weights fp16,
+// fp32 accumulation in TMEM, operands staged by TMA (128-byte swizzle) in a
+// STAGES-deep mbarrier ring, accumulators double-buffered in TMEM so the
+// epilogue of tile i overlaps the mainloop of tile i+1.
+//
+// Roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM owner + UMMA
+// issuer, warps 2..5 = epilogue (warp w reads TMEM lanes 32*(w%4)..+31).
+//
+// The epilogues fuse what the reference runs as separate ggml ops after each
+// mul_mat (src/vision_trunk.cpp:50-62 linear + bias, :451 gelu_erf, :439/:458
+// residual adds, :417-425 RoPE, :364-374 patch-embed + abs-pos, :461 NCHW
+// permute) and the activation rounding ggml's CPU mul_mat applies to the next
+// GEMM's input (fp16 for F16 weights, Q8_0 blocks for Q8_0 weights).
+#include "kernels.h"
+#include "ptx.cuh"
+
+#include <cuda_runtime.h>
+#include <stdio.h>
+
+namespace s3t {
+
+namespace {
+
+constexpr int kBM = 128, kBK = 64;
+
+template <int BN>
+struct GemmCfg {
+    static constexpr int STAGES = BN == 256 ? 4 : 6;
+    static constexpr uint32_t A_BYTES = kBM * kBK * 2;
+    static constexpr uint32_t B_BYTES = BN * kBK * 2;
+    static constexpr uint32_t TMEM_COLS = 2 * BN;
+    static constexpr size_t SMEM = size_t(STAGES) * (A_BYTES + B_BYTES) + 1024 + 256;
+};
+
+__device__ __forceinline__ void load_bias32(const float* bias, int n, float (&b)[32]) {
+    if (bias) {
+        const float4* p = reinterpret_cast<const float4*>(bias + n);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            float4 t = __ldg(p + i);
+            b[4 * i] = t.x; b[4 * i + 1] = t.y; b[4 * i + 2] = t.z; b[4 * i + 3] = t.w;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) b[i] = 0.f;
+    }
+}
+
+__device__ __forceinline__ void store_half32(__half* dst, const float (&v)[32]) {
+    uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        uint4 u;
+        u.x = pack_half2(v[8 * i + 0], v[8 * i + 1]);
+        u.y = pack_half2(v[8 * i + 2], v[8 * i + 3]);
+        u.z = pack_half2(v[8 * i + 4], v[8 * i + 5]);
+        u.w = pack_half2(v[8 * i + 6], v[8 * i + 7]);
+        d[i] = u;
+    }
+}
+
+template <int EPI>
+__device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int m, int n, const uint32_t (&r)[32]) {
+    float v[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+
+    if constexpr (EPI == kEpiF16) {
+        float b[32];
+        load_bias32(a.bias, n, b);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] += b[i];
+        if (a.gelu) {
+            // ggml_vec_gelu_erf_f32: 0.5*x*(1+erf(x/sqrt(2)))
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = 0.5f * v[i] * (1.0f + erff(v[i] * 0.70710678118654752440f));
+        }
+        if (a.q8) q8_0_fake_quant32(v);
+        store_half32(a.out16 + int64_t(m) * a.N + n, v);
+    } else if constexpr (EPI == kEpiQkv) {
+        float b[32];
+        load_bias32(a.bias, n, b);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] += b[i];
+        const int img = m / kTokens, t = m - img * kTokens;
+        const int y = t / kGrid, x = t - y * kGrid;
+        const int which = n >> 10, head = (n & 1023) >> 6, half = (n >> 5) & 1;
+        int g, i, L, px, py;
+        const float* tab;
+        if (a.windowed) {
+            g = img * 9 + (y / kWindow) * 3 + (x / kWindow);
+            py = y % kWindow; px = x % kWindow;
+            i = py * kWindow + px;
+            L = kWindow * kWindow;
+            tab = a.rope_local;
+        } else {
+            g = img; i = t; L = kTokens; px = x; py = y;
+            tab = a.rope_global;
+        }
+        if (which < 2) {
+            const float* cs = tab + (half ? py : px) * 32;   // [pos][cos16 | sin16]
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const float c = __ldg(cs + j), s = __ldg(cs + 16 + j);
+                const float x0 = v[2 * j], x1 = v[2 * j + 1];
+                v[2 * j] = x0 * c - x1 * s;
+                v[2 * j + 1] = x0 * s + x1 * c;
+            }
+        }
+        __half* dst = a.qkv + which * a.qkv_stride + (int64_t(g * kHeads + head) * L + i) * kHeadDim + half * 32;
+        store_half32(dst, v);
+    } else if constexpr (EPI == kEpiResid) {
+        float b[32];
+        load_bias32(a.bias, n, b);
+        float4* xr = reinterpret_cast<float4*>(a.resid + int64_t(m) * a.N + n);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            float4 t = xr[q];
+            t.x = t.x + (v[4 * q + 0] + b[4 * q + 0]);
+            t.y = t.y + (v[4 * q + 1] + b[4 * q + 1]);
+            t.z = t.z + (v[4 * q + 2] + b[4 * q + 2]);
+            t.w = t.w + (v[4 * q + 3] + b[4 * q + 3]);
+            xr[q] = t;
+            v[4 * q + 0] = t.x; v[4 * q + 1] = t.y; v[4 * q + 2] = t.z; v[4 * q + 3] = t.w;
+        }
+        if (a.out_nchw) {
+            const int img = m / kTokens, t = m - img * kTokens;
+            float* o = a.out_nchw + (int64_t(img) * a.N + n) * kTokens + t;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[int64_t(i) * kTokens] = v[i];
+        }
+    } else {  // kEpiPatch
+        const int t = m % kTokens;
+        const int y = t / kGrid, x = t - y * kGrid;
+        const float4* p = reinterpret_cast<const float4*>(a.pos + int64_t(1 + (y % 24) * 24 + (x % 24)) * kDim + n);
+        float4* xr = reinterpret_cast<float4*>(a.resid + int64_t(m) * a.N + n);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const float4 pp = __ldg(p + q);
+            xr[q] = make_float4(v[4 * q] + pp.x, v[4 * q + 1] + pp.y, v[4 * q + 2] + pp.z, v[4 * q + 3] + pp.w);
+        }
+    }
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(192, 1)
+    gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const GemmArgs args) {
+    using Cfg = GemmCfg<BN>;
+    constexpr int STAGES = Cfg::STAGES;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + STAGES * Cfg::A_BYTES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * Cfg::B_BYTES);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tfull = empty + STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint64_t* drain = tempty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_tiles_n = (args.N + BN - 1) / BN;
+    const int n_tiles = ((args.M + kBM - 1) / kBM) * n_tiles_n;
+    const int num_kb = args.K / kBK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(full + s, 1);
+            mbar_init(empty + s, 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(tfull + i, 1);
+            mbar_init(tempty + i, 4);
+        }
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            uint32_t armed = 0, armed_parity = 0;  // per-stage: armed at least once / parity of last arm
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
+                const int m0 = (tile / n_tiles_n) * kBM, n0 = (tile % n_tiles_n) * BN;
+                for (int kb = 0; kb < num_kb; ++kb) {
+                    if (!mbar_wait(empty + s, ph ^ 1, args.status, kErrTimeoutProducer, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(full + s, Cfg::A_BYTES + Cfg::B_BYTES);
+                    tma_load_2d(sA + s * Cfg::A_BYTES, &tmA, full + s, kb * kBK, m0);
+                    tma_load_2d(sB + s * Cfg::B_BYTES, &tmB, full + s, kb * kBK, n0);
+                    armed |= 1u << s;
+                    armed_parity = (armed_parity & ~(1u << s)) | (ph << s);
+                    if (++s == STAGES) {
+                        s = 0;
+                        ph ^= 1;
+                    }
+                }
+            }
+            if (!ok) {
+                // Gave up: wait (bounded) for the copies this thread started.
+                for (int i = 0; i < STAGES; ++i)
+                    if (armed & (1u << i))
+                        mbar_wait(full + i, (armed_parity >> i) & 1u, args.status, kErrTimeoutDrain, nullptr);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = umma_idesc_f16(kBM, BN, 0, 0);
+            int s = 0;
+            uint32_t ph = 0;
+            bool ok = true, issued = false;
+            int local = 0;
+            for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, ++local) {
+                const int acc = local & 1;
+                const uint32_t aph = (local >> 1) & 1;
+                if (!mbar_wait(tempty + acc, aph ^ 1, args.status, kErrTimeoutMma, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * BN;
+                for (int kb = 0; kb < num_kb; ++kb) {
+                    if (!mbar_wait(full + s, ph, args.status, kErrTimeoutMma, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(sA + s * Cfg::A_BYTES);
+                    const uint32_t b0 = smem_u32(sB + s * Cfg::B_BYTES);
+#pragma unroll
+                    for (int k = 0; k < kBK / 16; ++k) {
+                        umma_f16_ss(d_tmem, umma_desc_sw128(a0 + k * 32, 16, 1024), umma_desc_sw128(b0 + k * 32, 16, 1024),
+                                    idesc, (kb | k) != 0);
+                    }
+                    issued = true;
+                    umma_commit(empty + s);
+                    if (++s == STAGES) {
+                        s = 0;
+                        ph ^= 1;
+                    }
+                }
+                if (!ok) break;
+                umma_commit(tfull + acc);
+            }
+            if (!ok && issued) {
+                umma_commit(drain);
+                mbar_wait(drain, 0, args.status, kErrTimeoutDrain, nullptr);
+            }
+        }
+    } else {
+        const int quarter = warp & 3;
+        const int row = quarter * 32 + lane;
+        int local = 0;
+        for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++local) {
+            const int acc = local & 1;
+            const uint32_t aph = (local >> 1) & 1;
+            if (!mbar_wait(tfull + acc, aph, args.status, kErrTimeoutEpilogue, abort_flag)) break;
+            tc_fence_after();
+            const int m0 = (tile / n_tiles_n) * kBM, n0 = (tile % n_tiles_n) * BN;
+            const int m = m0 + row;
+            const uint32_t tbase = tmem_base + (uint32_t(quarter * 32) << 16) + acc * BN;
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                const int n = n0 + c * 32;
+                if (n >= args.N) break;
+                uint32_t r[32];
+                tmem_ld32(tbase + c * 32, r);
+                tmem_wait_ld();
+                if (m < args.M) epilogue_chunk<EPI>(args, m, n, r);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(tempty + acc);
+        }
+    }
+
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+    }
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+template <int BN, int EPI>
+cudaError_t launch_bn(const __half* A, const __half* B, const GemmArgs& args, int num_sms, cudaStream_t stream) {
+    using Cfg = GemmCfg<BN>;
+    CUtensorMap ta, tb;
+    if (!make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, args.K, args.M, kBK, kBM)) return cudaErrorInvalidValue;
+    if (!make_tmap_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, args.K, args.N, kBK, BN)) return cudaErrorInvalidValue;
+    auto kern = gemm_tn_kernel<BN, EPI>;
+    const int n_tiles = ((args.M + kBM - 1) / kBM) * ((args.N + BN - 1) / BN);
+    const int grid = n_tiles < num_sms ? n_tiles : num_sms;
+    kern<<<grid, 192, Cfg::SMEM, stream>>>(ta, tb, args);
+    return cudaGetLastError();
+}
+
+template <int BN, int EPI>
+cudaError_t prepare_bn() {
+    return cudaFuncSetAttribute(gemm_tn_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(GemmCfg<BN>::SMEM));
+}
+
+}  // namespace
+
+cudaError_t gemm_prepare() {
+    cudaError_t e;
+    if ((e = prepare_bn<256, kEpiF16>()) != cudaSuccess) return e;
+    if ((e = prepare_bn<128, kEpiF16>()) != cudaSuccess) return e;
+    if ((e = prepare_bn<256, kEpiQkv>()) != cudaSuccess) return e;
+    if ((e = prepare_bn<256, kEpiResid>()) != cudaSuccess) return e;
+    if ((e = prepare_bn<128, kEpiResid>()) != cudaSuccess) return e;
+    return prepare_bn<256, kEpiPatch>();
+}
+
+bool make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,
+                  uint64_t outer, uint32_t box_inner, uint32_t box_outer) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {inner * uint64_t(elem_bytes)};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t d0,
+                  uint64_t d1, uint64_t d2, uint32_t b0, uint32_t b1) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[3] = {d0, d1, d2};
+    cuuint64_t strides[2] = {d0 * uint64_t(elem_bytes), d0 * d1 * uint64_t(elem_bytes)};
+    cuuint32_t box[3] = {b0, b1, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return fn(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+cudaError_t launch_gemm(const __half* A, const __half* B, const GemmArgs& args, int epi, int num_sms,
+                        cudaStream_t stream) {
+    if (args.K % kBK != 0 || args.N % 32 != 0 || args.M <= 0) return cudaErrorInvalidValue;
+    if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B)) & 15) return cudaErrorInvalidValue;
+    // N = 1024 / 3072 / 4736: 256-wide tiles (4736 leaves one half tile);
+    // narrow problems use 128-wide tiles.
+    const bool wide = args.N >= 1024;
+    switch (epi) {
+        case kEpiF16:
+            return wide ? launch_bn<256, kEpiF16>(A, B, args, num_sms, stream)
+                        : launch_bn<128, kEpiF16>(A, B, args, num_sms, stream);
+        case kEpiQkv:
+            return launch_bn<256, kEpiQkv>(A, B, args, num_sms, stream);
+        case kEpiResid:
+            return wide ? launch_bn<256, kEpiResid>(A, B, args, num_sms, stream)
+                        : launch_bn<128, kEpiResid>(A, B, args, num_sms, stream);
+        case kEpiPatch:
+            return launch_bn<256, kEpiPatch>(A, B, args, num_sms, stream);
+    }
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace s3t

@@ -1,0 +1,104 @@
+// Host-side launch interface of the trunk kernels (sm_100a).  Every launcher
+// returns a cudaError_t and never synchronizes.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace s3t {
+
+constexpr int kImage = 1008, kPatch = 14, kGrid = 72, kTokens = 5184, kDim = 1024;
+constexpr int kHeads = 16, kHeadDim = 64, kMlp = 4736, kLayers = 32, kWindow = 24;
+constexpr int kPatchK = 3 * 14 * 14;       // 588
+constexpr int kPatchKPad = 640;            // padded to the 64-wide K block
+
+// Error codes written to the device status word (first writer wins).
+enum : int {
+    kErrNone = 0,
+    kErrTimeoutProducer = 1,
+    kErrTimeoutMma = 2,
+    kErrTimeoutEpilogue = 3,
+    kErrTimeoutDrain = 4,
+};
+
+enum GemmEpilogue : int {
+    kEpiF16 = 0,     // out16 = act(acc + bias) [optional GELU, optional Q8_0 rounding]
+    kEpiQkv = 1,     // acc + bias, RoPE on q/k, scattered into the attention layout
+    kEpiResid = 2,   // x += acc + bias (fp32 residual), optional NCHW copy
+    kEpiPatch = 3,   // x = acc + tiled pos_embed (fp32)
+};
+
+struct GemmArgs {
+    int M, N, K;
+    const float* bias;        // [N] or null
+    __half* out16;            // kEpiF16: [M][N]
+    int gelu;                 // kEpiF16: apply GELU (erf)
+    int q8;                   // kEpiF16: Q8_0 activation rounding of the output
+    float* resid;             // kEpiResid / kEpiPatch: x [M][N] fp32
+    float* out_nchw;          // kEpiResid: also write [img][N][5184] (or null)
+    const float* pos;         // kEpiPatch: pos_embed [577][1024]
+    __half* qkv;              // kEpiQkv: q block; k at +qkv_stride, v at +2*qkv_stride
+    int64_t qkv_stride;
+    int windowed;             // kEpiQkv: 24x24 windows (1) or whole image (0)
+    const float* rope_local;  // [24][2][16] cos,sin for scale 1
+    const float* rope_global; // [72][2][16] cos,sin for scale 24/72
+    int* status;              // device status word
+};
+
+// C[M,N] = A[M,K] * B[N,K]^T with A, B fp16 row-major (K contiguous).
+// Requires K % 64 == 0 and N % 32 == 0; A and B 16-byte aligned rows.
+cudaError_t launch_gemm(const __half* A, const __half* B, const GemmArgs& args, int epi, int num_sms,
+                        cudaStream_t stream);
+
+struct AttnArgs {
+    const void* q;            // [groups*16][L][64]
+    const void* k;
+    const void* v;
+    int groups;               // images * windows-per-image
+    int L;                    // tokens per group (576 windowed, 5184 global)
+    int windowed;             // output token mapping
+    float scale_log2;         // softmax scale * log2(e)
+    int bf16;                 // operand type: fp16 (0) or bf16 (1)
+    int q8;                   // Q8_0 activation rounding of the output
+    void* out;                // [images*5184][1024] (fp16 or bf16), token-major, natural order
+    int* status;
+};
+
+cudaError_t launch_attention(const AttnArgs& args, cudaStream_t stream);
+
+// Row LayerNorm over 1024 columns (eps 1e-5).  Mode 0: y16 = LN(x); mode 1
+// (stem): x = LN_a(x) kept in fp32, then y16 = LN_b(x).
+cudaError_t launch_layernorm(const float* x, int rows, const float* g, const float* b, __half* y16, int q8,
+                             cudaStream_t stream);
+cudaError_t launch_layernorm_stem(float* x, int rows, const float* g0, const float* b0, const float* g1,
+                                  const float* b1, __half* y16, int q8, cudaStream_t stream);
+
+// images [B][3][1008][1008] fp32 -> patches [B*5184][640] fp16, column
+// ic*196 + kh*14 + kw, zero beyond 588.  round_f16: the pixel values become
+// fp16 (true for every weight format: the MMA operands are fp16).
+cudaError_t launch_im2col(const float* images, int batch, __half* cols, cudaStream_t stream);
+
+// Weight preparation (once per model).
+cudaError_t launch_dequant_q8_0_to_f16(const uint8_t* blocks, int64_t n, __half* out, cudaStream_t stream);
+cudaError_t launch_dequant_q8_0_to_f32(const uint8_t* blocks, int64_t n, float* out, cudaStream_t stream);
+cudaError_t launch_f16_to_f32(const __half* in, int64_t n, float* out, cudaStream_t stream);
+cudaError_t launch_f32_to_f16(const float* in, int64_t n, __half* out, cudaStream_t stream);
+
+// Standalone axial RoPE on [groups*16][L][64] (attention microbench input).
+cudaError_t launch_rope_inplace(void* x, int groups, int L, int windowed, int bf16, const float* rope_local,
+                                const float* rope_global, cudaStream_t stream);
+
+// Per-device one-time setup (dynamic shared-memory limits); call with the
+// device current before the first launch and outside stream capture.
+cudaError_t gemm_prepare();
+cudaError_t attention_prepare();
+
+// Tensor-map creation through the driver entry point.
+bool make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,
+                  uint64_t outer, uint32_t box_inner, uint32_t box_outer);
+bool make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t d0,
+                  uint64_t d1, uint64_t d2, uint32_t b0, uint32_t b1);
+
+}  // namespace s3t

@@ -1,0 +1,128 @@
+"""Generate the golden fixtures in tests/golden/ from the reference itself.
+
+Runs where the reference sources are available (oracle/_ref built by
+`make -C oracle ref`): every expected value here is computed by the
+reference's own code — ggml's CPU ops for the op-level vectors and
+sam3::VisionTrunk::run for the full-trunk outputs — on seeded inputs.
+
+    python tests/golden/make_golden.py            # op vectors + all three trunks
+    python tests/golden/make_golden.py --ops-only
+
+Files:
+  ops.npz                   inputs and ggml outputs of small op cases
+  trunk_<fmt>_img0.npz      32-layer output on the seeded <fmt> file and image 0:
+                            every STRIDE-th element, plus mean/std of all of it
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+ROOT = HERE.parents[1]
+sys.path.insert(0, str(ROOT))
+
+from oracle.pyoracle import F16, F32, Q8_0, Reference  # noqa: E402
+from sam3cpp_b200 import synthetic as s  # noqa: E402
+
+STRIDE = 61
+
+
+def op_vectors(ref: Reference) -> dict[str, np.ndarray]:
+    rng = np.random.default_rng(2024)
+    out: dict[str, np.ndarray] = {}
+    x = (rng.standard_normal(4096) * 3).astype(np.float32)
+    x[::97] = 0
+    x[:8] = [65519.9, 65520.0, 1e-6, 6e-8, -3e-5, 2.5e-8, -65504.0, 7e-5]
+    out["fp16_in"] = x
+    out["fp16_out"] = ref.fp16(x)
+    out["q8act_in"] = x
+    out["q8act_out"] = ref.quantize_q8_0_act(x)
+    w = (rng.standard_normal((96, 256)) * 0.02).astype(np.float32)
+    w[0, :32] = 0
+    qw = s.quantize_q8_0_rows(w)
+    out["q8w_bytes"] = qw
+    out["q8w_f32"] = ref.to_float(Q8_0, qw, w.size)
+    xa = rng.standard_normal((37, 256)).astype(np.float32)
+    out["mm_x"] = xa
+    out["mm_w_f32"] = w
+    out["mm_w_f16"] = w.astype(np.float16).view(np.uint16)
+    out["mm_w_q8"] = qw
+    out["mm_y_f32"] = ref.mul_mat(F32, w, 96, 256, xa)
+    out["mm_y_f16"] = ref.mul_mat(F16, out["mm_w_f16"], 96, 256, xa)
+    out["mm_y_q8"] = ref.mul_mat(Q8_0, qw, 96, 256, xa)
+    xn = (rng.standard_normal((16, 1024)) * 2 + 0.3).astype(np.float32)
+    out["norm_x"] = xn
+    out["norm_y"] = ref.norm(xn)
+    # RoPE at window-local (24x24) positions and at a sample of the 72x72 grid
+    xr = rng.standard_normal((576, 2, 64)).astype(np.float32)
+    pos = np.arange(576)
+    out["rope_x"] = xr
+    out["rope_local"] = ref.rope_axial(xr, pos % 24, pos // 24, 1.0)
+    pg = rng.choice(5184, 400, replace=False)
+    out["rope_gpos"] = pg.astype(np.int32)
+    xg = rng.standard_normal((400, 2, 64)).astype(np.float32)
+    out["rope_gx"] = xg
+    out["rope_global"] = ref.rope_axial(xg, pg % 72, pg // 72, np.float32(24) / np.float32(72))
+    q, k, v = (rng.standard_normal((192, 2, 64)).astype(np.float32) for _ in range(3))
+    out["fa_q"], out["fa_k"], out["fa_v"] = q, k, v
+    out["fa_out"] = ref.flash_attn(q, k, v, 0.125)
+    g = (rng.standard_normal(4000) * 3).astype(np.float32)
+    out["gelu_x"] = g
+    out["gelu_y"] = ref.gelu_erf(g)
+    # patch embed of image 0 with seeded F16 weights (weights regenerated
+    # from the seed by the test; every 997th output element stored)
+    prng = np.random.default_rng(77)
+    pw = (prng.standard_normal((1024, 14, 14, 3)) * 0.02).astype(np.float32).astype(np.float16)
+    img = s.synthetic_image(0)
+    pe16 = ref.patch_embed(F16, pw.view(np.uint16), img)
+    out["patch_y_f16_sample"] = pe16.reshape(-1)[::997]
+    return out
+
+
+def trunk_golden(ref: Reference, fmt: str, threads: int) -> dict:
+    path = s.synthetic_gguf(fmt)
+    img = s.synthetic_image(0)
+    t0 = time.time()
+    y, sec = ref.trunk(path, img, threads)
+    flat = y.reshape(-1)
+    return {
+        "sample": flat[::STRIDE].astype(np.float32),
+        "stride": np.int64(STRIDE),
+        "mean": np.float64(flat.astype(np.float64).mean()),
+        "std": np.float64(flat.astype(np.float64).std()),
+        "absmax": np.float64(np.abs(flat).max()),
+        "run_seconds": np.float64(sec),
+        "threads": np.int64(threads),
+        "wall": np.float64(time.time() - t0),
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ops-only", action="store_true")
+    ap.add_argument("--formats", default="f16,q8_0,f32")
+    ap.add_argument("--threads", type=int, default=8)
+    a = ap.parse_args()
+    ref = Reference()
+    np.savez_compressed(HERE / "ops.npz", **op_vectors(ref))
+    print("ops.npz written")
+    if a.ops_only:
+        return
+    meta = {}
+    for fmt in a.formats.split(","):
+        g = trunk_golden(ref, fmt, a.threads)
+        np.savez_compressed(HERE / f"trunk_{fmt}_img0.npz", **g)
+        meta[fmt] = {k: float(v) for k, v in g.items() if k != "sample"}
+        print(fmt, meta[fmt], flush=True)
+    (HERE / "trunk_meta.json").write_text(json.dumps({"reference": str(ref.path.name), **meta}, indent=2))
+
+
+if __name__ == "__main__":
+    main()
