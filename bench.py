@@ -124,6 +124,13 @@ def run_ours(a):
     if world > 1:
         import datetime
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+    # A real (non-default) stream: the trunk, torch's events and the gather
+    # all run on it.
+    with torch.cuda.stream(torch.cuda.Stream(dev)):
+        _run_ours(a, torch, dist, world, rank, local, dev)
+
+
+def _run_ours(a, torch, dist, world, rank, local, dev):
 
     import sam3cpp_b200 as s3t
     from sam3cpp_b200 import synthetic as syn

@@ -47,6 +47,10 @@ class Oracle:
         L.or_gelu_erf.argtypes = [_p, _i64, _p]
         L.or_patch_embed.argtypes = [C.c_int, _p, _p, _p]
         L.or_trunk_run.argtypes = [_p, _p, C.c_int, _p, _p]
+        L.or_set_sum_variant.argtypes = [C.c_int]
+
+    def set_sum_variant(self, v: int):
+        self.lib.or_set_sum_variant(v)
 
     def fp16(self, x):
         x = np.ascontiguousarray(x, np.float32)

@@ -130,8 +130,33 @@ void or_round_activations(int wtype, const float *x, int64_t n, float *y) {
 
 /* ------------------------------------------------------------- linear --- */
 
+/* Summation-order variant of the dot products (0: ascending K, 1: descending
+ * K).  Both are equally faithful to ggml; comparing them measures how much a
+ * trunk result moves under a pure change of floating-point summation order. */
+static int g_sum_variant = 0;
+void or_set_sum_variant(int v) { g_sum_variant = v; }
+
+static void gemm_nt_rev(const float *x, const float *w, int64_t M, int64_t N, int64_t K,
+                        const float *bias, float *y) {
+#pragma omp parallel for schedule(dynamic, 4)
+    for (int64_t m = 0; m < M; m++) {
+        const float *x0 = x + m * K;
+        for (int64_t n = 0; n < N; n++) {
+            const float *wr = w + n * K;
+            float a0 = 0;
+#pragma omp simd reduction(+ : a0)
+            for (int64_t k = K - 1; k >= 0; k--) a0 += x0[k] * wr[k];
+            y[m * N + n] = a0 + (bias ? bias[n] : 0.0f);
+        }
+    }
+}
+
 static void gemm_nt(const float *x, const float *w, int64_t M, int64_t N, int64_t K,
                     const float *bias, float *y) {
+    if (g_sum_variant) {
+        gemm_nt_rev(x, w, M, N, K, bias, y);
+        return;
+    }
     const int64_t MB = 16, NB = 64;
 #pragma omp parallel for schedule(dynamic, 1) collapse(2)
     for (int64_t m0 = 0; m0 < M; m0 += MB) {

@@ -26,6 +26,7 @@ void     or_dequantize(int type, const void *src, int64_t n, float *y);
 void     or_quantize_q8_0_act(const float *x, int64_t n, uint8_t *blocks);
 void     or_round_activations(int wtype, const float *x, int64_t n, float *y);
 
+void or_set_sum_variant(int variant);
 void or_linear(int wtype, const void *w, int64_t N, int64_t K, const float *x, int64_t M,
                const float *bias, float *y);
 void or_layer_norm(const float *x, int64_t rows, int64_t cols, const float *gamma,

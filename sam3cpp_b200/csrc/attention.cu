@@ -8,16 +8,22 @@
 // q/k/v arrive grouped per (window, head) and the output is written back to
 // natural token order, so no permute copy exists.
 //
-// One CTA = one 128-query tile of one (group, head).  Roles (192 threads):
-// warp 0 TMA producer (Q once, K/V 64-key blocks into a 3-deep ring), warp 1
-// TMEM owner + UMMA issuer, warps 2..5 softmax (one query row per thread).
+// Persistent kernel: each CTA walks a static list of work items (128-query
+// tile, head, group).  Roles (192 threads): warp 0 TMA producer, warp 1 TMEM
+// owner + UMMA issuer, warps 2..5 softmax + epilogue (one query row per
+// thread).  Per 64-key block b of an item:
 //   S = Q K^T   : UMMA M=128 N=64 K=64, accumulator in TMEM cols [0,64)
-//   P = exp2(S*scale*log2e - m) written as fp16/bf16 into a swizzled smem tile
-//   O += P V    : UMMA M=128 N=64 K=64 (V MN-major), accumulator in TMEM [64,128)
-// S_{j+1} is issued as soon as the softmax warps have read S_j, so the tensor
-// core overlaps the exponentials; O is rescaled in TMEM when the row max grows.
+//   P = 2^(S*scale*log2e - m) as fp16/bf16 into a 128-byte-swizzled smem tile
+//   O += P V    : UMMA M=128 N=64 K=64 (V MN-major) into TMEM O[item & 1]
+// The UMMA issuer runs one block ahead (S_{b+1} is issued as soon as S_b has
+// been read), across item boundaries too; Q and O are double-buffered so the
+// next item's loads and first S overlap the current item's epilogue.  The row
+// max used for P is raised only when a block exceeds it by more than 2^8 (O
+// is then rescaled in TMEM).  Shared memory (96 KB) and registers are sized
+// for two CTAs per SM; a 3-deep K/V ring keeps S_{b+1} from waiting on loads.
 // L is a multiple of 64 for both layer kinds, so keys are never masked; query
-// rows past L (last tile) are computed on zero-filled Q rows and not stored.
+// rows past L (last tile of a group) are computed on zero-filled Q rows and
+// not stored.
 #include "kernels.h"
 #include "ptx.cuh"
 
@@ -29,8 +35,9 @@ constexpr int kBQ = 128, kBKV = 64, kD = 64, kKVStages = 3;
 constexpr uint32_t kQBytes = kBQ * kD * 2;      // 16 KB
 constexpr uint32_t kKVBytes = kBKV * kD * 2;    // 8 KB (each of K, V)
 constexpr uint32_t kPBytes = kBQ * kBKV * 2;    // 16 KB
-constexpr size_t kAttnSmem = kQBytes + 2 * kKVStages * kKVBytes + kPBytes + 1024 + 256;
-constexpr uint32_t kAttnTmemCols = 128;
+constexpr size_t kAttnSmem = 2 * kQBytes + 2 * kKVStages * kKVBytes + kPBytes + 1024 + 256;
+constexpr uint32_t kAttnTmemCols = 256;         // S [0,64), O0 [64,128), O1 [128,192)
+constexpr int kCtasPerSm = 2;
 
 template <int BF16>
 __device__ __forceinline__ uint32_t pack2(float a, float b) {
@@ -38,35 +45,55 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
     else return pack_half2(a, b);
 }
 
+struct Item {
+    int qt, head, grp;
+};
+
+__device__ __forceinline__ Item item_of(int w, int n_qt) {
+    Item it;
+    it.qt = w % n_qt;
+    const int r = w / n_qt;
+    it.head = r % kHeads;
+    it.grp = r / kHeads;
+    return it;
+}
+
 template <int BF16>
-__global__ void __launch_bounds__(192, 2)
+__global__ void __launch_bounds__(192, kCtasPerSm)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const AttnArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* sQ = smem;
-    uint8_t* sK = sQ + kQBytes;
+    uint8_t* sQ = smem;                              // 2 buffers
+    uint8_t* sK = sQ + 2 * kQBytes;
     uint8_t* sV = sK + kKVStages * kKVBytes;
     uint8_t* sP = sV + kKVStages * kKVBytes;
     uint64_t* bars = reinterpret_cast<uint64_t*>(sP + kPBytes);
-    uint64_t* q_full = bars;
-    uint64_t* kv_full = bars + 1;
-    uint64_t* kv_empty = kv_full + kKVStages;
+    uint64_t* q_full = bars;                         // [2]
+    uint64_t* q_empty = q_full + 2;                  // [2]
+    uint64_t* kv_full = q_empty + 2;                 // [S]
+    uint64_t* kv_empty = kv_full + kKVStages;        // [S]
     uint64_t* s_full = kv_empty + kKVStages;
     uint64_t* s_free = s_full + 1;
     uint64_t* p_full = s_free + 1;
-    uint64_t* o_done = p_full + 1;
-    uint64_t* drain = o_done + 1;
+    uint64_t* o_done = p_full + 1;                   // [2]: PV of blocks with that parity
+    uint64_t* o_free = o_done + 2;                   // [2]
+    uint64_t* drain = o_free + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int qt = blockIdx.x, head = blockIdx.y, grp = blockIdx.z;
-    const int bh = grp * kHeads + head;
     const int nkv = a.L / kBKV;
+    const int n_qt = (a.L + kBQ - 1) / kBQ;
+    const int n_items = n_qt * kHeads * a.groups;
 
     if (threadIdx.x == 0) {
-        mbar_init(q_full, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(q_full + i, 1);
+            mbar_init(q_empty + i, 1);
+            mbar_init(o_free + i, 4);
+            mbar_init(o_done + i, 1);
+        }
         for (int s = 0; s < kKVStages; ++s) {
             mbar_init(kv_full + s, 1);
             mbar_init(kv_empty + s, 1);
@@ -74,7 +101,6 @@ __global__ void __launch_bounds__(192, 2)
         mbar_init(s_full, 1);
         mbar_init(s_free, 4);
         mbar_init(p_full, 4);
-        mbar_init(o_done, 1);
         mbar_init(drain, 1);
         *abort_flag = 0;
         fence_barrier_init();
@@ -92,29 +118,46 @@ __global__ void __launch_bounds__(192, 2)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t tS = tmem, tO = tmem + 64;
+    const uint32_t tS = tmem;
 
     if (warp == 0) {
         if (lane == 0) {
-            uint32_t armed = 0, armed_parity = 0;
+            uint32_t armed = 0, armed_parity = 0, q_armed = 0, q_parity = 0;
             bool ok = true;
-            mbar_arrive_expect_tx(q_full, kQBytes);
-            tma_load_3d(sQ, &tmQ, q_full, 0, qt * kBQ, bh);
-            for (int j = 0; j < nkv; ++j) {
-                const int s = j % kKVStages;
-                const uint32_t ph = (j / kKVStages) & 1;
-                if (!mbar_wait(kv_empty + s, ph ^ 1, a.status, kErrTimeoutProducer, abort_flag)) {
+            int b = 0;   // global block counter of this CTA
+            int li = 0;  // local item counter
+            for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++li) {
+                const Item it = item_of(w, n_qt);
+                const int bh = it.grp * kHeads + it.head;
+                const int qb = li & 1;
+                const uint32_t qph = (li >> 1) & 1;
+                if (!mbar_wait(q_empty + qb, qph ^ 1, a.status, kErrTimeoutProducer, abort_flag)) {
                     ok = false;
                     break;
                 }
-                mbar_arrive_expect_tx(kv_full + s, 2 * kKVBytes);
-                tma_load_3d(sK + s * kKVBytes, &tmK, kv_full + s, 0, j * kBKV, bh);
-                tma_load_3d(sV + s * kKVBytes, &tmV, kv_full + s, 0, j * kBKV, bh);
-                armed |= 1u << s;
-                armed_parity = (armed_parity & ~(1u << s)) | (ph << s);
+                mbar_arrive_expect_tx(q_full + qb, kQBytes);
+                tma_load_3d(sQ + qb * kQBytes, &tmQ, q_full + qb, 0, it.qt * kBQ, bh);
+                q_armed |= 1u << qb;
+                q_parity = (q_parity & ~(1u << qb)) | (qph << qb);
+                for (int j = 0; j < nkv; ++j, ++b) {
+                    const int s = b % kKVStages;
+                    const uint32_t ph = (b / kKVStages) & 1;
+                    if (!mbar_wait(kv_empty + s, ph ^ 1, a.status, kErrTimeoutProducer, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(kv_full + s, 2 * kKVBytes);
+                    tma_load_3d(sK + s * kKVBytes, &tmK, kv_full + s, 0, j * kBKV, bh);
+                    tma_load_3d(sV + s * kKVBytes, &tmV, kv_full + s, 0, j * kBKV, bh);
+                    armed |= 1u << s;
+                    armed_parity = (armed_parity & ~(1u << s)) | (ph << s);
+                }
             }
             if (!ok) {
-                mbar_wait(q_full, 0, a.status, kErrTimeoutDrain, nullptr);
+                // Gave up: wait (bounded) for every copy this thread started.
+                for (int i = 0; i < 2; ++i)
+                    if (q_armed & (1u << i))
+                        mbar_wait(q_full + i, (q_parity >> i) & 1u, a.status, kErrTimeoutDrain, nullptr);
                 for (int i = 0; i < kKVStages; ++i)
                     if (armed & (1u << i))
                         mbar_wait(kv_full + i, (armed_parity >> i) & 1u, a.status, kErrTimeoutDrain, nullptr);
@@ -124,42 +167,54 @@ __global__ void __launch_bounds__(192, 2)
         if (lane == 0) {
             constexpr uint32_t idS = umma_idesc_f16(kBQ, kBKV, BF16, 0);
             constexpr uint32_t idO = umma_idesc_f16(kBQ, kD, BF16, 1);
-            const uint32_t q0 = smem_u32(sQ), p0 = smem_u32(sP);
+            const int my_items = int(blockIdx.x) < n_items ? (n_items - 1 - int(blockIdx.x)) / int(gridDim.x) + 1 : 0;
+            const int total = my_items * nkv;
             bool ok = true, issued = false;
-            auto issue_s = [&](int j) -> bool {
-                const int s = j % kKVStages;
-                if (!mbar_wait(kv_full + s, (j / kKVStages) & 1, a.status, kErrTimeoutMma, abort_flag)) return false;
-                if (j > 0 && !mbar_wait(s_free, (j - 1) & 1, a.status, kErrTimeoutMma, abort_flag)) return false;
+            // S for this CTA's global block b (item b / nkv, key block b % nkv)
+            auto issue_s = [&](int b) -> bool {
+                const int li = b / nkv, j = b - li * nkv, s = b % kKVStages;
+                const int qb = li & 1;
+                if (j == 0 && !mbar_wait(q_full + qb, (li >> 1) & 1, a.status, kErrTimeoutMma, abort_flag))
+                    return false;
+                if (!mbar_wait(kv_full + s, (b / kKVStages) & 1, a.status, kErrTimeoutMma, abort_flag)) return false;
+                if (b > 0 && !mbar_wait(s_free, (b - 1) & 1, a.status, kErrTimeoutMma, abort_flag)) return false;
                 tc_fence_after();
-                const uint32_t k0 = smem_u32(sK + s * kKVBytes);
+                const uint32_t q0 = smem_u32(sQ + qb * kQBytes), k0 = smem_u32(sK + s * kKVBytes);
 #pragma unroll
                 for (int k = 0; k < kD / 16; ++k)
-                    umma_f16_ss(tS, umma_desc_sw128(q0 + k * 32, 16, 1024), umma_desc_sw128(k0 + k * 32, 16, 1024), idS,
-                                k != 0);
+                    umma_f16_ss(tS, umma_desc_sw128(q0 + k * 32, 16, 1024), umma_desc_sw128(k0 + k * 32, 16, 1024),
+                                idS, k != 0);
                 umma_commit(s_full);
+                if (j == nkv - 1) umma_commit(q_empty + qb);   // Q buffer reusable once these S complete
                 issued = true;
                 return true;
             };
-            if (!mbar_wait(q_full, 0, a.status, kErrTimeoutMma, abort_flag)) ok = false;
-            if (ok) ok = issue_s(0);
-            for (int j = 0; ok && j < nkv; ++j) {
-                if (j + 1 < nkv && !issue_s(j + 1)) {
+            if (total > 0) ok = issue_s(0);
+            for (int b = 0; ok && b < total; ++b) {
+                if (b + 1 < total && !issue_s(b + 1)) {
                     ok = false;
                     break;
                 }
-                if (!mbar_wait(p_full, j & 1, a.status, kErrTimeoutMma, abort_flag)) {
+                const int li = b / nkv, j = b - li * nkv, s = b % kKVStages;
+                const int ob = li & 1;
+                if (!mbar_wait(p_full, b & 1, a.status, kErrTimeoutMma, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                if (j == 0 && !mbar_wait(o_free + ob, ((li >> 1) & 1) ^ 1, a.status, kErrTimeoutMma, abort_flag)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const int s = j % kKVStages;
                 const uint32_t v0 = smem_u32(sV + s * kKVBytes);
+                const uint32_t p0 = smem_u32(sP);
+                const uint32_t tO = tmem + 64 + ob * 64;
 #pragma unroll
                 for (int k = 0; k < kBKV / 16; ++k)
                     umma_f16_ss(tO, umma_desc_sw128(p0 + k * 32, 16, 1024),
                                 umma_desc_sw128(v0 + k * 16 * 128, kKVBytes, 1024), idO, (j | k) != 0);
                 umma_commit(kv_empty + s);
-                umma_commit(o_done);
+                umma_commit(o_done + (b & 1));
             }
             if (!ok && issued) {
                 umma_commit(drain);
@@ -171,82 +226,114 @@ __global__ void __launch_bounds__(192, 2)
         const int row = quarter * 32 + lane;
         const uint32_t lane_off = uint32_t(quarter * 32) << 16;
         const float sl2 = a.scale_log2;
-        float m_run = -INFINITY, l_run = 0.f;
+        // m_run is the (log2-domain) max the P values of this row are taken
+        // relative to.  It is only raised when a block's max exceeds it by
+        // more than kRescaleSlack, so O is rescaled in TMEM rarely; P values
+        // stay <= 2^kRescaleSlack, and O / l is unchanged by the choice.
+        constexpr float kRescaleSlack = 8.0f;
         bool ok = true;
-        for (int j = 0; j < nkv; ++j) {
-            if (!mbar_wait(s_full, j & 1, a.status, kErrTimeoutEpilogue, abort_flag)) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            uint32_t r0[32], r1[32];
-            tmem_ld32(tS + lane_off, r0);
-            tmem_ld32(tS + lane_off + 32, r1);
-            tmem_wait_ld();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(s_free);
-
-            float mx = -INFINITY;
-#pragma unroll
-            for (int i = 0; i < 32; ++i) mx = fmaxf(mx, fmaxf(__uint_as_float(r0[i]), __uint_as_float(r1[i])));
-            const float m_new = fmaxf(m_run, mx * sl2);
-            const float alpha = ex2_approx(m_run - m_new);
-            float sum = 0.f;
-            uint32_t pk[32];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                const float e0 = ex2_approx(fmaf(__uint_as_float(r0[2 * i]), sl2, -m_new));
-                const float e1 = ex2_approx(fmaf(__uint_as_float(r0[2 * i + 1]), sl2, -m_new));
-                const float f0 = ex2_approx(fmaf(__uint_as_float(r1[2 * i]), sl2, -m_new));
-                const float f1 = ex2_approx(fmaf(__uint_as_float(r1[2 * i + 1]), sl2, -m_new));
-                sum += (e0 + e1) + (f0 + f1);
-                pk[i] = pack2<BF16>(e0, e1);
-                pk[16 + i] = pack2<BF16>(f0, f1);
-            }
-            l_run = l_run * alpha + sum;
-
-            if (j > 0) {
-                if (!mbar_wait(o_done, (j - 1) & 1, a.status, kErrTimeoutEpilogue, abort_flag)) {
+        int b = 0, li = 0;
+        for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++li) {
+            const Item it = item_of(w, n_qt);
+            const int ob = li & 1;
+            const uint32_t tO = tmem + 64 + ob * 64;
+            float m_run = -INFINITY, l_run = 0.f;
+            for (int j = 0; j < nkv; ++j, ++b) {
+                if (!mbar_wait(s_full, b & 1, a.status, kErrTimeoutEpilogue, abort_flag)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                if (__any_sync(0xffffffffu, alpha < 1.0f)) {
-                    uint32_t o0[32], o1[32];
-                    tmem_ld32(tO + lane_off, o0);
-                    tmem_ld32(tO + lane_off + 32, o1);
-                    tmem_wait_ld();
+                uint32_t r[64];
+                tmem_ld32(tS + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+                tmem_ld32(tS + lane_off + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+                tmem_wait_ld();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(s_free);
+
+                float acc[8];
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        o0[i] = __float_as_uint(__uint_as_float(o0[i]) * alpha);
-                        o1[i] = __float_as_uint(__uint_as_float(o1[i]) * alpha);
-                    }
-                    tmem_st32(tO + lane_off, o0);
-                    tmem_st32(tO + lane_off + 32, o1);
-                    tmem_wait_st();
+                for (int i = 0; i < 8; ++i)
+                    acc[i] = fmax3(__uint_as_float(r[i]), __uint_as_float(r[8 + i]), __uint_as_float(r[16 + i]));
+#pragma unroll
+                for (int i = 24; i < 64; i += 16)
+#pragma unroll
+                    for (int k = 0; k < 8; ++k)
+                        acc[k] = fmax3(acc[k], __uint_as_float(r[i + k]), __uint_as_float(r[i + 8 + k]));
+                const float mx =
+                    fmax3(fmax3(acc[0], acc[1], acc[2]), fmax3(acc[3], acc[4], acc[5]), fmaxf(acc[6], acc[7])) * sl2;
+                const bool raise = mx > m_run + kRescaleSlack;
+                const float m_new = raise ? mx : m_run;
+                const float alpha = raise ? ex2_approx(m_run - m_new) : 1.0f;
+                uint32_t pk[32];
+                float sums[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    const float e0 = ex2_approx(fmaf(__uint_as_float(r[2 * i]), sl2, -m_new));
+                    const float e1 = ex2_approx(fmaf(__uint_as_float(r[2 * i + 1]), sl2, -m_new));
+                    sums[i & 3] += e0 + e1;
+                    pk[i] = pack2<BF16>(e0, e1);
                 }
-            }
-            // P row -> 128-byte swizzled smem row (16-byte chunk c at c ^ (row & 7)).
-            uint8_t* prow = sP + row * 128;
+                l_run = l_run * alpha + ((sums[0] + sums[1]) + (sums[2] + sums[3]));
+
+                // The P tile is free once the PV of block b-1 has completed.
+                if (b > 0) {
+                    if (!mbar_wait(o_done + ((b - 1) & 1), ((b - 1) >> 1) & 1, a.status, kErrTimeoutEpilogue, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                }
+                // Rescaling O needs the PV of block b-1 (same item) to have completed.
+                if (j > 0 && __any_sync(0xffffffffu, raise)) {
+                    if (!mbar_wait(o_done + ((b - 1) & 1), ((b - 1) >> 1) & 1, a.status, kErrTimeoutEpilogue,
+                                   abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    {
+                        uint32_t o0[32], o1[32];
+                        tmem_ld32(tO + lane_off, o0);
+                        tmem_ld32(tO + lane_off + 32, o1);
+                        tmem_wait_ld();
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                uint4 u = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-                *reinterpret_cast<uint4*>(prow + ((c ^ (row & 7)) << 4)) = u;
+                        for (int i = 0; i < 32; ++i) {
+                            o0[i] = __float_as_uint(__uint_as_float(o0[i]) * alpha);
+                            o1[i] = __float_as_uint(__uint_as_float(o1[i]) * alpha);
+                        }
+                        tmem_st32(tO + lane_off, o0);
+                        tmem_st32(tO + lane_off + 32, o1);
+                        tmem_wait_st();
+                    }
+                }
+                // P row -> 128-byte swizzled smem row (16-byte chunk c at c ^ (row & 7)).
+                uint8_t* prow = sP + row * 128;
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    uint4 u = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+                    *reinterpret_cast<uint4*>(prow + ((c ^ (row & 7)) << 4)) = u;
+                }
+                fence_proxy_async_smem();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(p_full);
+                m_run = m_new;
             }
-            fence_proxy_async_smem();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(p_full);
-            m_run = m_new;
-        }
-        if (ok && mbar_wait(o_done, (nkv - 1) & 1, a.status, kErrTimeoutEpilogue, abort_flag)) {
+            if (!ok || !mbar_wait(o_done + ((b - 1) & 1), ((b - 1) >> 1) & 1, a.status, kErrTimeoutEpilogue, abort_flag)) {
+                ok = false;
+                break;
+            }
+            // Item epilogue: O / l, natural token order.
             tc_fence_after();
             uint32_t o0[32], o1[32];
             tmem_ld32(tO + lane_off, o0);
             tmem_ld32(tO + lane_off + 32, o1);
             tmem_wait_ld();
-            const int qi = qt * kBQ + row;
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(o_free + ob);
+            const int qi = it.qt * kBQ + row;
             if (qi < a.L) {
                 const float inv = 1.0f / l_run;
                 float v[2][32];
@@ -261,16 +348,16 @@ __global__ void __launch_bounds__(192, 2)
                 }
                 int img, tok;
                 if (a.windowed) {
-                    img = grp / 9;
-                    const int w = grp - img * 9, wy = w / 3, wx = w - wy * 3;
+                    img = it.grp / 9;
+                    const int wi = it.grp - img * 9, wy = wi / 3, wx = wi - wy * 3;
                     const int ly = qi / kWindow, lx = qi - ly * kWindow;
                     tok = (wy * kWindow + ly) * kGrid + wx * kWindow + lx;
                 } else {
-                    img = grp;
+                    img = it.grp;
                     tok = qi;
                 }
                 uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.out) +
-                                                      (int64_t(img) * kTokens + tok) * kDim + head * kD);
+                                                      (int64_t(img) * kTokens + tok) * kDim + it.head * kD);
 #pragma unroll
                 for (int h = 0; h < 2; ++h)
 #pragma unroll
@@ -306,7 +393,11 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t stream) {
     if (!make_tmap_3d(&tq, a.q, dt, 2, kD, a.L, zdim, kD, kBQ)) return cudaErrorInvalidValue;
     if (!make_tmap_3d(&tk, a.k, dt, 2, kD, a.L, zdim, kD, kBKV)) return cudaErrorInvalidValue;
     if (!make_tmap_3d(&tv, a.v, dt, 2, kD, a.L, zdim, kD, kBKV)) return cudaErrorInvalidValue;
-    dim3 grid((a.L + kBQ - 1) / kBQ, kHeads, a.groups);
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int n_items = ((a.L + kBQ - 1) / kBQ) * kHeads * a.groups;
+    const int grid = n_items < sms * kCtasPerSm ? n_items : sms * kCtasPerSm;
     if (a.bf16)
         attn_fwd_kernel<1><<<grid, 192, kAttnSmem, stream>>>(tq, tk, tv, a);
     else

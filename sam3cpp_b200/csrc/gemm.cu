@@ -72,9 +72,8 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int m, int n, 
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] += b[i];
         if (a.gelu) {
-            // ggml_vec_gelu_erf_f32: 0.5*x*(1+erf(x/sqrt(2)))
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = 0.5f * v[i] * (1.0f + erff(v[i] * 0.70710678118654752440f));
+            for (int i = 0; i < 32; ++i) v[i] = gelu_erf_as(v[i]);
         }
         if (a.q8) q8_0_fake_quant32(v);
         store_half32(a.out16 + int64_t(m) * a.N + n, v);

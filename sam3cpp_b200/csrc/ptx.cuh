@@ -195,6 +195,32 @@ S3T_DEV void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
         : "memory");
 }
 
+S3T_DEV void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+}
+
+S3T_DEV void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+        "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+
+// Three-input max (sm_100).
+S3T_DEV float fmax3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
 S3T_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 S3T_DEV void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -203,6 +229,49 @@ S3T_DEV float ex2_approx(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
+}
+
+// 1/x on the SFU (hardware approximation).
+S3T_DEV float rcp_approx(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// 2^x for x <= 0 on the FMA/ALU pipes, used for a share of the softmax
+// exponentials so the SFU is not the only unit doing them (the split used
+// by FlashAttention-4).  Range reduction x = n + f, n = round(x), f in
+// [-1/2, 1/2]; 2^f by a degree-4 polynomial whose coefficients are this
+// project's own minimax fit of relative error on that interval (max 2.7e-6
+// in fp32); 2^n applied by adding n to the exponent field.
+S3T_DEV float exp2_poly(float x) {
+    x = fmaxf(x, -125.0f);
+    const float magic = 12582912.0f;  // 1.5 * 2^23: x + magic rounds x to an integer
+    const float t = x + magic;
+    const float n = t - magic;
+    const float f = x - n;
+    float p = fmaf(9.569674936e-03f, f, 5.591824792e-02f);
+    p = fmaf(p, f, 2.402476669e-01f);
+    p = fmaf(p, f, 6.931217338e-01f);
+    p = fmaf(p, f, 9.999992361e-01f);
+    const int ni = __float_as_int(t) - __float_as_int(magic);
+    return __int_as_float(__float_as_int(p) + (ni << 23));
+}
+
+// GELU with the error function of Abramowitz & Stegun, Handbook of
+// Mathematical Functions, formula 7.1.26 (|erf error| <= 1.5e-7):
+// erf(z) = 1 - (a1 t + ... + a5 t^5) exp(-z^2), t = 1/(1 + p z), z >= 0.
+// Same function as ggml_vec_gelu_erf_f32: 0.5 x (1 + erf(x / sqrt 2)).
+S3T_DEV float gelu_erf_as(float x) {
+    const float z = fabsf(x) * 0.70710678118654752f;
+    const float t = rcp_approx(fmaf(0.3275911f, z, 1.0f));
+    float q = fmaf(1.061405429f, t, -1.453152027f);
+    q = fmaf(q, t, 1.421413741f);
+    q = fmaf(q, t, -0.284496736f);
+    q = fmaf(q, t, 0.254829592f);
+    q = q * t * ex2_approx(-z * z * 1.44269504088896341f);   // poly(t) * exp(-z^2)
+    const float one_plus_erf = x >= 0.f ? 2.0f - q : q;
+    return 0.5f * x * one_plus_erf;
 }
 
 S3T_DEV uint32_t pack_half2(float a, float b) {

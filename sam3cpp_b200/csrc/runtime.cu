@@ -8,7 +8,7 @@
 // (im2col, patch GEMM, stem LayerNorms, then per block: QKV GEMM + RoPE,
 // attention, proj GEMM + residual, LayerNorm, fc1 GEMM + GELU, fc2 GEMM +
 // residual + next LayerNorm).
-#include "../../include/s3t.h"
+#include "s3t.h"
 #include "kernels.h"
 
 #include <cuda_runtime.h>

@@ -104,6 +104,20 @@ def trunk_golden(ref: Reference, fmt: str, threads: int) -> dict:
     }
 
 
+def isa_spread(fmt: str, threads: int, gold: dict) -> dict:
+    """Distance between two builds of the same reference code on the same file:
+    the AVX2 build (libsam3ref_v3) against the golden AVX-512 build (v4).
+    They differ only in SIMD summation order; for Q8_0 weights the activation
+    re-quantization before every GEMM amplifies that into a large spread."""
+    v3 = Reference(HERE.parents[1] / "oracle" / "_ref" / "libsam3ref_v3.so")
+    y, _ = v3.trunk(s.synthetic_gguf(fmt), s.synthetic_image(0), threads)
+    smp = y.reshape(-1)[::STRIDE].astype(np.float64)
+    ref = gold["sample"].astype(np.float64)
+    rel = float(np.linalg.norm(smp - ref) / np.linalg.norm(ref))
+    cos = float(smp @ ref / (np.linalg.norm(smp) * np.linalg.norm(ref)))
+    return {"isa_spread_rel_l2": np.float64(rel), "isa_spread_cos": np.float64(cos)}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ops-only", action="store_true")
@@ -118,6 +132,7 @@ def main():
     meta = {}
     for fmt in a.formats.split(","):
         g = trunk_golden(ref, fmt, a.threads)
+        g.update(isa_spread(fmt, a.threads, g))
         np.savez_compressed(HERE / f"trunk_{fmt}_img0.npz", **g)
         meta[fmt] = {k: float(v) for k, v in g.items() if k != "sample"}
         print(fmt, meta[fmt], flush=True)
