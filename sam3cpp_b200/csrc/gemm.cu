@@ -300,6 +300,196 @@ __global__ void __launch_bounds__(192, 1)
     }
 }
 
+// Two-SM version: a CTA pair (cluster of 2) owns a 256 x 256 output tile
+// (320 threads per CTA: producer warp, MMA warp, 8 epilogue warps).
+// CTA r stages rows [128r, 128r+128) of the A tile and rows [128r, 128r+128)
+// of the B tile (half of N); the leader (rank 0) issues
+// tcgen05.mma.cta_group::2 (M=256, N=256), which reads both CTAs' halves and
+// leaves rows [128r, +128) x 256 of the accumulator in CTA r's TMEM.  Each
+// UMMA therefore reads 8 KB of a CTA's shared memory per 128 x 256 x 16 of
+// work instead of 12 KB.  Loads of both CTAs complete on the leader's full
+// barrier; the leader's commits arrive on both CTAs' barriers (multicast
+// commit); both CTAs' epilogue warps release an accumulator buffer on the
+// leader's barrier.  No TMA load uses cluster multicast.
+struct PairCfg {
+    static constexpr int BN = 256;
+    static constexpr int STAGES = 6;
+    static constexpr uint32_t A_BYTES = kBM * kBK * 2;          // this CTA's 128 rows of A
+    static constexpr uint32_t B_BYTES = (BN / 2) * kBK * 2;     // this CTA's 128 rows of B
+    static constexpr uint32_t TMEM_COLS = 2 * BN;
+    static constexpr size_t SMEM = size_t(STAGES) * (A_BYTES + B_BYTES) + 1024 + 256;
+    static constexpr int EPI_WARPS = 8;
+    static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+};
+
+template <int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg::THREADS, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const GemmArgs args) {
+    using Cfg = PairCfg;
+    constexpr int STAGES = Cfg::STAGES, BN = Cfg::BN;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + STAGES * Cfg::A_BYTES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * Cfg::B_BYTES);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tfull = empty + STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint64_t* drain = tempty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const int n_tiles_n = (args.N + BN - 1) / BN;
+    const int n_tiles = ((args.M + 2 * kBM - 1) / (2 * kBM)) * n_tiles_n;
+    const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
+    const int num_kb = args.K / kBK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(full + s, 1);
+            mbar_init(empty + s, 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(tfull + i, 1);
+            mbar_init(tempty + i, 2 * PairCfg::EPI_WARPS);   // every epilogue warp of the pair
+        }
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync();   // both CTAs' barriers exist before any cross-CTA arrive
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            uint32_t armed = 0, armed_parity = 0;
+            bool ok = true;
+            for (int tile = pair; tile < n_tiles && ok; tile += n_pairs) {
+                const int m0 = (tile / n_tiles_n) * 2 * kBM + int(rank) * kBM;
+                const int n0 = (tile % n_tiles_n) * BN + int(rank) * (BN / 2);
+                for (int kb = 0; kb < num_kb; ++kb) {
+                    if (!mbar_wait(empty + s, ph ^ 1, args.status, kErrTimeoutProducer, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t lfull = mapa_shared(smem_u32(full + s), 0);
+                    if (leader) {
+                        mbar_arrive_expect_tx(full + s, 2 * (Cfg::A_BYTES + Cfg::B_BYTES));
+                        armed |= 1u << s;
+                        armed_parity = (armed_parity & ~(1u << s)) | (ph << s);
+                    }
+                    tma_load_2d_pair(sA + s * Cfg::A_BYTES, &tmA, lfull, kb * kBK, m0);
+                    tma_load_2d_pair(sB + s * Cfg::B_BYTES, &tmB, lfull, kb * kBK, n0);
+                    if (++s == STAGES) {
+                        s = 0;
+                        ph ^= 1;
+                    }
+                }
+            }
+            if (!ok && leader) {
+                // Gave up: wait (bounded) for the pair's copies counted on these barriers.
+                for (int i = 0; i < STAGES; ++i)
+                    if (armed & (1u << i))
+                        mbar_wait(full + i, (armed_parity >> i) & 1u, args.status, kErrTimeoutDrain, nullptr);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && leader) {
+            constexpr uint32_t idesc = umma_idesc_f16(2 * kBM, BN, 0, 0);
+            int s = 0;
+            uint32_t ph = 0;
+            bool ok = true, issued = false;
+            int local = 0;
+            for (int tile = pair; tile < n_tiles && ok; tile += n_pairs, ++local) {
+                const int acc = local & 1;
+                const uint32_t aph = (local >> 1) & 1;
+                if (!mbar_wait(tempty + acc, aph ^ 1, args.status, kErrTimeoutMma, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * BN;
+                for (int kb = 0; kb < num_kb; ++kb) {
+                    if (!mbar_wait(full + s, ph, args.status, kErrTimeoutMma, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(sA + s * Cfg::A_BYTES);
+                    const uint32_t b0 = smem_u32(sB + s * Cfg::B_BYTES);
+#pragma unroll
+                    for (int k = 0; k < kBK / 16; ++k)
+                        umma_f16_ss_pair(d_tmem, umma_desc_sw128(a0 + k * 32, 16, 1024),
+                                         umma_desc_sw128(b0 + k * 32, 16, 1024), idesc, (kb | k) != 0);
+                    issued = true;
+                    umma_commit_pair(empty + s, 0x3);
+                    if (++s == STAGES) {
+                        s = 0;
+                        ph ^= 1;
+                    }
+                }
+                if (!ok) break;
+                umma_commit_pair(tfull + acc, 0x3);
+            }
+            if (!ok && issued) {
+                umma_commit_pair(drain, 0x1);
+                mbar_wait(drain, 0, args.status, kErrTimeoutDrain, nullptr);
+            }
+        }
+    } else {
+        // Epilogue warps 2..9: warp w reads TMEM lane quarter w % 4 (rows
+        // 32*(w%4)..+31 of this CTA's half) and half of the 256 columns.
+        const int quarter = warp & 3;
+        const int col_half = (warp - 2) >> 2;
+        const int row = quarter * 32 + lane;
+        int local = 0;
+        for (int tile = pair; tile < n_tiles; tile += n_pairs, ++local) {
+            const int acc = local & 1;
+            const uint32_t aph = (local >> 1) & 1;
+            if (!mbar_wait(tfull + acc, aph, args.status, kErrTimeoutEpilogue, abort_flag)) break;
+            tc_fence_after();
+            const int m = (tile / n_tiles_n) * 2 * kBM + int(rank) * kBM + row;
+            const int n0 = (tile % n_tiles_n) * BN + col_half * (BN / 2);
+            const uint32_t tbase = tmem_base + (uint32_t(quarter * 32) << 16) + acc * BN + col_half * (BN / 2);
+#pragma unroll 1
+            for (int c = 0; c < BN / 64; ++c) {
+                const int n = n0 + c * 32;
+                if (n >= args.N) break;
+                uint32_t r[32];
+                tmem_ld32(tbase + c * 32, r);
+                tmem_wait_ld();
+                if (m < args.M) epilogue_chunk<EPI>(args, m, n, r);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(tempty + acc), 0));
+        }
+    }
+
+    tc_fence_before();
+    cluster_sync();   // no CTA leaves while its pair may still signal or read it
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
+    }
+}
+
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -329,6 +519,29 @@ cudaError_t launch_bn(const __half* A, const __half* B, const GemmArgs& args, in
     return cudaGetLastError();
 }
 
+// Co-resident CTA pairs of the pair kernel on the current device (set by
+// gemm_prepare; one process drives one device at a time in this library).
+int g_pair_capacity = 0;
+
+template <int EPI>
+cudaError_t launch_pair(const __half* A, const __half* B, const GemmArgs& args, int num_sms, cudaStream_t stream) {
+    CUtensorMap ta, tb;
+    if (!make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, args.K, args.M, kBK, kBM)) return cudaErrorInvalidValue;
+    if (!make_tmap_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, args.K, args.N, kBK, PairCfg::BN / 2))
+        return cudaErrorInvalidValue;
+    const int n_tiles = ((args.M + 2 * kBM - 1) / (2 * kBM)) * ((args.N + PairCfg::BN - 1) / PairCfg::BN);
+    // Persistent grid: only as many pairs as can be resident at once.
+    const int max_pairs = g_pair_capacity > 0 ? g_pair_capacity : num_sms / 2;
+    const int pairs = n_tiles < max_pairs ? n_tiles : max_pairs;
+    gemm_pair_kernel<EPI><<<2 * pairs, PairCfg::THREADS, PairCfg::SMEM, stream>>>(ta, tb, args);
+    return cudaGetLastError();
+}
+
+template <int EPI>
+cudaError_t prepare_pair() {
+    return cudaFuncSetAttribute(gemm_pair_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(PairCfg::SMEM));
+}
+
 template <int BN, int EPI>
 cudaError_t prepare_bn() {
     return cudaFuncSetAttribute(gemm_tn_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -344,7 +557,31 @@ cudaError_t gemm_prepare() {
     if ((e = prepare_bn<256, kEpiQkv>()) != cudaSuccess) return e;
     if ((e = prepare_bn<256, kEpiResid>()) != cudaSuccess) return e;
     if ((e = prepare_bn<128, kEpiResid>()) != cudaSuccess) return e;
-    return prepare_bn<256, kEpiPatch>();
+    if ((e = prepare_bn<256, kEpiPatch>()) != cudaSuccess) return e;
+    if ((e = prepare_pair<kEpiF16>()) != cudaSuccess) return e;
+    {
+        int dev = 0, sms = 0, clusters = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(sms, 1, 1);
+        cfg.blockDim = dim3(PairCfg::THREADS, 1, 1);
+        cfg.dynamicSmemBytes = PairCfg::SMEM;
+        cudaLaunchAttribute attr;
+        attr.id = cudaLaunchAttributeClusterDimension;
+        attr.val.clusterDim.x = 2;
+        attr.val.clusterDim.y = 1;
+        attr.val.clusterDim.z = 1;
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        if (cudaOccupancyMaxActiveClusters(&clusters, gemm_pair_kernel<kEpiF16>, &cfg) == cudaSuccess && clusters > 0)
+            g_pair_capacity = clusters;
+        else
+            g_pair_capacity = sms / 2;
+    }
+    if ((e = prepare_pair<kEpiQkv>()) != cudaSuccess) return e;
+    if ((e = prepare_pair<kEpiResid>()) != cudaSuccess) return e;
+    return prepare_pair<kEpiPatch>();
 }
 
 bool make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,
@@ -377,9 +614,18 @@ cudaError_t launch_gemm(const __half* A, const __half* B, const GemmArgs& args, 
                         cudaStream_t stream) {
     if (args.K % kBK != 0 || args.N % 32 != 0 || args.M <= 0) return cudaErrorInvalidValue;
     if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B)) & 15) return cudaErrorInvalidValue;
-    // N = 1024 / 3072 / 4736: 256-wide tiles (4736 leaves one half tile);
-    // narrow problems use 128-wide tiles.
+    // N = 1024 / 3072 / 4736: CTA-pair 256 x 256 tiles (4736 leaves one half
+    // tile); narrow problems use single-CTA 128 x 128 tiles.
     const bool wide = args.N >= 1024;
+    if (wide && num_sms >= 2) {
+        switch (epi) {
+            case kEpiF16: return launch_pair<kEpiF16>(A, B, args, num_sms, stream);
+            case kEpiQkv: return launch_pair<kEpiQkv>(A, B, args, num_sms, stream);
+            case kEpiResid: return launch_pair<kEpiResid>(A, B, args, num_sms, stream);
+            case kEpiPatch: return launch_pair<kEpiPatch>(A, B, args, num_sms, stream);
+        }
+        return cudaErrorInvalidValue;
+    }
     switch (epi) {
         case kEpiF16:
             return wide ? launch_bn<256, kEpiF16>(A, B, args, num_sms, stream)
