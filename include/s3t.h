@@ -108,6 +108,22 @@ int s3t_layernorm(int device, const float *x, int rows, const float *gamma, cons
  * the op-level entry points write when a bounded in-kernel wait times out. */
 int s3t_device_status(int device);
 
+/* Allocation-free stem (no counterpart in the reference): patch embedding +
+ * tiled position embedding + ln_pre for one image, the same values as
+ * s3t_trunk_run_layers(ctx, ..., n_layers = 0, ...) but token-major:
+ * images_dev [batch][3][1008][1008] fp32 -> out_tokens_dev [batch*5184][1024]
+ * fp32, both device pointers on the context's GPU, enqueued on `stream`
+ * (NULL = the legacy default stream).  For callers that cannot call
+ * cudaMalloc (plugins whose host application owns all device memory, loops
+ * with a fixed memory budget): it allocates nothing; its one scratch buffer
+ * is a static device array inside the library sized for batch <= 1
+ * (6,635,520 bytes, held by every GPU that loads the library until exit).
+ * Larger batches are rejected with an error.  The first call on a device
+ * looks up that array's device address; make that first call before any
+ * stream capture.  Calls whose work overlaps on the same GPU race on the
+ * shared array. */
+int s3t_stem_noalloc(s3t_ctx *ctx, const float *images_dev, int batch, float *out_tokens_dev, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -64,6 +64,7 @@ def lib() -> C.CDLL:
         L.s3t_rope.argtypes = [i, p, i, i, i, i, p]
         L.s3t_layernorm.argtypes = [i, p, i, p, p, p, i, p]
         L.s3t_device_status.argtypes = [i]
+        L.s3t_stem_noalloc.argtypes = [p, p, i, p, p]
         _lib = L
     return _lib
 

@@ -95,10 +95,29 @@ cudaError_t launch_rope_inplace(void* x, int groups, int L, int windowed, int bf
 cudaError_t gemm_prepare();
 cudaError_t attention_prepare();
 
+// Stem weights of a finalized context, for entry points defined outside
+// runtime.cu.  Returns false if the context is null or not finalized.
+struct StemView {
+    int device;
+    int num_sms;
+    const __half* patch_w;   // [1024][640] fp16, column ic*196 + kh*14 + kw
+    const float* pos;        // [577][1024]
+    const float* ln_w;
+    const float* ln_b;
+    int* status;
+};
+
 // Tensor-map creation through the driver entry point.
 bool make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,
                   uint64_t outer, uint32_t box_inner, uint32_t box_outer);
 bool make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t d0,
                   uint64_t d1, uint64_t d2, uint32_t b0, uint32_t b1);
 
+}  // namespace s3t
+
+struct s3t_ctx;
+namespace s3t {
+bool ctx_stem_view(const s3t_ctx* ctx, StemView* out);
+// Records the thread-local message returned by s3t_last_error(); returns -1.
+int set_last_error(const char* msg);
 }  // namespace s3t

@@ -506,6 +506,20 @@ int upload_f32_vec(s3t_ctx* c, const Staged& s, int64_t n, float** dst) {
 
 }  // namespace
 
+int s3t::set_last_error(const char* msg) { return fail(msg); }
+
+bool s3t::ctx_stem_view(const s3t_ctx* c, StemView* out) {
+    if (!c || !c->finalized || !out) return false;
+    out->device = c->device;
+    out->num_sms = c->dev->num_sms;
+    out->patch_w = c->patch_w;
+    out->pos = c->pos;
+    out->ln_w = c->lnpre_w;
+    out->ln_b = c->lnpre_b;
+    out->status = c->dev->status;
+    return true;
+}
+
 extern "C" {
 
 const char* s3t_last_error(void) { return g_last_error.c_str(); }
