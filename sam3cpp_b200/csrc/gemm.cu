@@ -98,13 +98,18 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int m, int n, 
             tab = a.rope_global;
         }
         if (which < 2) {
-            const float* cs = tab + (half ? py : px) * 32;   // [pos][cos16 | sin16]
+            const float4* cs = reinterpret_cast<const float4*>(tab + (half ? py : px) * 32);   // [pos][cos16 | sin16]
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                const float c = __ldg(cs + j), s = __ldg(cs + 16 + j);
-                const float x0 = v[2 * j], x1 = v[2 * j + 1];
-                v[2 * j] = x0 * c - x1 * s;
-                v[2 * j + 1] = x0 * s + x1 * c;
+            for (int q = 0; q < 4; ++q) {
+                const float4 c4 = __ldg(cs + q), s4 = __ldg(cs + 4 + q);
+                const float c[4] = {c4.x, c4.y, c4.z, c4.w}, s[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int j = 4 * q + u;
+                    const float x0 = v[2 * j], x1 = v[2 * j + 1];
+                    v[2 * j] = x0 * c[u] - x1 * s[u];
+                    v[2 * j + 1] = x0 * s[u] + x1 * c[u];
+                }
             }
         }
         __half* dst = a.qkv + which * a.qkv_stride + (int64_t(g * kHeads + head) * L + i) * kHeadDim + half * 32;
@@ -462,10 +467,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg::THREADS, 1)
         for (int tile = pair; tile < n_tiles; tile += n_pairs, ++local) {
             const int acc = local & 1;
             const uint32_t aph = (local >> 1) & 1;
-            if (!mbar_wait(tfull + acc, aph, args.status, kErrTimeoutEpilogue, abort_flag)) break;
-            tc_fence_after();
             const int m = (tile / n_tiles_n) * 2 * kBM + int(rank) * kBM + row;
             const int n0 = (tile % n_tiles_n) * BN + col_half * (BN / 2);
+            if constexpr (EPI == kEpiResid) {
+                // Pull this thread's residual slice (128 fp32 = 4 lines) into L2
+                // while the tile's mainloop is still running.
+                if (m < args.M) {
+                    const float* xr = args.resid + int64_t(m) * args.N + n0;
+#pragma unroll
+                    for (int q = 0; q < 4; ++q)
+                        if (n0 + 32 * q < args.N) prefetch_l2(xr + 32 * q);
+                }
+            }
+            if (!mbar_wait(tfull + acc, aph, args.status, kErrTimeoutEpilogue, abort_flag)) break;
+            tc_fence_after();
             const uint32_t tbase = tmem_base + (uint32_t(quarter * 32) << 16) + acc * BN + col_half * (BN / 2);
 #pragma unroll 1
             for (int c = 0; c < BN / 64; ++c) {

@@ -121,9 +121,17 @@ S3T_DEV void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
-// Arrive on an mbarrier given by its shared::cluster address (possibly the peer's).
+// Arrive on an mbarrier given by its shared::cluster address (possibly the
+// peer's), with the default release-at-CTA-scope semantics: enough to order
+// this warp's completed TMEM reads (tcgen05.fence::before_thread_sync) before
+// the MMA that reuses the accumulator, without waiting for the warp's global
+// stores to drain as a cluster-scope release would.
 S3T_DEV void mbar_arrive_cluster(uint32_t cluster_addr) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+S3T_DEV void prefetch_l2(const void* p) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
 
 // TMA tile load into this CTA's shared memory whose completion is counted on
