@@ -38,6 +38,10 @@ METRIC = "ViT-trunk images/s @1008^2"
 FLOP_PER_IMAGE = 5.3986e12          # GEMMs 4609.6 GF + attention 782.8 GF + patch 6.24 GF
 GEMM_FLOP_PER_IMAGE_LAYER = 144.05e9  # 2*T*C*(3C + C + 2F), T=5184, C=1024, F=4736
 LAUNCHES_PER_TRUNK = 3 + 32 * 6 + 31  # im2col, patch GEMM, stem LN; 6 per block; 31 inter-block LNs
+# DRAM bytes (read + write) of the four GEMM launches of one block, per image:
+# ncu capture of the 4-image trunk (profiles/gemm_pair_4img.md: 122 + 161 +
+# 198 + 362 MB), scaled by the images a launch processes.
+GEMM_DRAM_BYTES_PER_IMAGE_LAYER = 843e6 / 4
 
 
 def measured_peaks():
@@ -240,10 +244,11 @@ def _run_ours(a, torch, dist, world, rank, local, dev):
         },
         "roofline": {
             "bound": "tensor",
-            "kernel": "gemm_tn_kernel (qkv+proj+fc1+fc2 of one block, M=%d)" % (per * 5184),
+            "kernel": "gemm_pair_kernel (qkv+proj+fc1+fc2 of one block, M=%d)" % (per * 5184),
             "achieved": round(achieved, 1), "peak": bf16_peak, "unit": "TFLOP/s",
             "frac": round(achieved / bf16_peak, 4), "peak_kind": f"{peak_kind} bf16 burst",
-            "traffic": kern.get("traffic"),
+            "traffic": GEMM_DRAM_BYTES_PER_IMAGE_LAYER * per,
+            "traffic_note": "bytes per block's four GEMM launches; ncu 4-image capture scaled by images",
             "per_gemm_ms": kern["per_gemm_ms"],
             "trunk_tensor_frac": round(FLOP_PER_IMAGE * value / world / 1e12 / bf16_peak, 4),
         },
@@ -315,9 +320,44 @@ def _event_ms(torch, dev, stream, fn, warm, reps):
     return e0.elapsed_time(e1) / reps
 
 
+def attention_microbench(torch, dev, stream, images=32):
+    """Attention-only microbenchmark in bf16 with axial RoPE on Q and K:
+    windowed (images x 9 windows x 576 tokens x 16 heads x d64) and global
+    (images x 5184 tokens x 16 heads x d64), Q/K/V ~ N(0, 1) from seed 5."""
+    import ctypes as C
+    from sam3cpp_b200 import lib, check
+    L = lib()
+    peak = measured_peaks()[0]
+    g = torch.Generator(device=dev).manual_seed(5)
+    res = {}
+    for kind, (groups, Lk, win) in {"windowed": (9 * images, 576, 1), "global": (images, 5184, 0)}.items():
+        q, k, v = (torch.randn((groups * 16, Lk, 64), generator=g, device=dev, dtype=torch.bfloat16) for _ in range(3))
+        o = torch.empty((images * 5184, 1024), device=dev, dtype=torch.bfloat16)
+        sp = C.c_void_p(stream.cuda_stream)
+
+        def rope():
+            check(L.s3t_rope(dev.index, C.c_void_p(q.data_ptr()), groups, Lk, win, 1, sp))
+            check(L.s3t_rope(dev.index, C.c_void_p(k.data_ptr()), groups, Lk, win, 1, sp))
+
+        def attn():
+            check(L.s3t_attention(dev.index, C.c_void_p(q.data_ptr()), C.c_void_p(k.data_ptr()),
+                                  C.c_void_p(v.data_ptr()), groups, Lk, win, 1, C.c_void_p(o.data_ptr()), sp))
+
+        ms_attn = _event_ms(torch, dev, stream, attn, 3, 10)
+        ms_both = _event_ms(torch, dev, stream, lambda: (rope(), attn()), 2, 5)
+        flop = 4.0 * groups * 16 * Lk * Lk * 64
+        res[kind] = {"shape": f"{groups}x16x{Lk}x64", "attention_ms": round(ms_attn, 4),
+                     "tflops": round(flop / (ms_attn / 1e3) / 1e12, 1),
+                     "frac_of_bf16_peak": round(flop / (ms_attn / 1e3) / 1e12 / peak, 4),
+                     "with_rope_ms": round(ms_both, 4)}
+        del q, k, v, o
+    check(L.s3t_device_status(dev.index))
+    return res
+
+
 def config_extras(torch, dev, stream, trunk, syn, s3t):
-    """Single-GPU extras: b=1 F16 p50 latency (device in -> device out) and
-    Q8_0 batch-8 throughput."""
+    """Single-GPU extras: b=1 F16 p50 latency (device in -> device out),
+    Q8_0 batch-8 throughput and the bf16 attention microbenchmark."""
     img = torch.from_numpy(syn.synthetic_images(1)).to(dev)
     out = torch.empty((1, 1024, 72, 72), device=dev)
     lat = []
@@ -343,6 +383,7 @@ def config_extras(torch, dev, stream, trunk, syn, s3t):
         qm.close()
     except Exception as e:  # reported, not fatal for the headline line
         res["q8_0_b8_error"] = str(e)
+    res["attention_microbench_bf16"] = attention_microbench(torch, dev, stream)
     return res
 
 

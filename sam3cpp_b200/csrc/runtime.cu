@@ -17,6 +17,7 @@
 #include <sys/stat.h>
 #include <unistd.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -278,6 +279,8 @@ struct s3t_ctx {
     float *img = nullptr, *out = nullptr;
 
     std::map<GraphKey, cudaGraphExec_t> graphs;
+    cudaStream_t copy_in = nullptr, copy_out = nullptr;   // host-buffer pipelining
+    std::vector<cudaEvent_t> events;
 };
 
 namespace {
@@ -437,28 +440,9 @@ int check_status(s3t_ctx* c, cudaStream_t st) {
     return 0;
 }
 
-int run_impl(s3t_ctx* c, const float* images, int batch, int n_layers, float* out, int flags, void* stream) {
-    if (!c) return fail("ctx is null");
-    if (!c->finalized) return fail("weights not finalized (call s3t_finalize_weights)");
-    if (!images || !out) return fail("images or out is null");
-    if (batch <= 0) return fail("batch must be positive");
-    if (n_layers < 0 || n_layers > c->n_layers) return fail("n_layers out of range");
-    S3T_CUDA(cudaSetDevice(c->device));
-    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : c->stream;
-    if (ensure_workspace(c, batch)) return -1;
-
-    const bool in_dev = flags & S3T_IMAGES_ON_DEVICE, out_dev = flags & S3T_OUTPUT_ON_DEVICE;
-    const size_t in_bytes = size_t(batch) * 3 * kImage * kImage * 4;
-    const size_t out_bytes = size_t(batch) * kDim * kTokens * 4;
-    const float* din = in_dev ? images : c->img;
-    float* dout = out_dev ? out : c->out;
-    if (!in_dev) S3T_CUDA(cudaMemcpyAsync(c->img, images, in_bytes, cudaMemcpyHostToDevice, st));
-
-    if (n_layers == 0) {
-        if (run_stem(c, din, batch, out, out_dev, st)) return -1;
-        return check_status(c, st);
-    }
-
+// The captured CUDA graph of the trunk for (batch, n_layers, input, output),
+// captured on first use.
+int trunk_graph(s3t_ctx* c, const float* din, int batch, int n_layers, float* dout, cudaGraphExec_t* out) {
     const GraphKey key{batch, n_layers, din, dout};
     auto it = c->graphs.find(key);
     if (it == c->graphs.end()) {
@@ -480,7 +464,86 @@ int run_impl(s3t_ctx* c, const float* images, int batch, int n_layers, float* ou
         S3T_CUDA(ei);
         it = c->graphs.emplace(key, exec).first;
     }
-    S3T_CUDA(cudaGraphLaunch(it->second, st));
+    *out = it->second;
+    return 0;
+}
+
+// Images per pipelined chunk when both buffers are on the host.
+constexpr int kHostChunk = 8;
+
+int ensure_events(s3t_ctx* c, size_t n) {
+    while (c->events.size() < n) {
+        cudaEvent_t e;
+        S3T_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+        c->events.push_back(e);
+    }
+    if (!c->copy_in) S3T_CUDA(cudaStreamCreateWithFlags(&c->copy_in, cudaStreamNonBlocking));
+    if (!c->copy_out) S3T_CUDA(cudaStreamCreateWithFlags(&c->copy_out, cudaStreamNonBlocking));
+    return 0;
+}
+
+// Host images -> host features for several chunks: the upload of chunk k+1
+// and the download of chunk k-1 run on their own streams (their own copy
+// engines) while the trunk runs chunk k on `st`, so only the first upload
+// and the last download are not hidden behind compute.
+int run_host_pipelined(s3t_ctx* c, const float* images, int batch, int n_layers, float* out, cudaStream_t st) {
+    const int nc = (batch + kHostChunk - 1) / kHostChunk;
+    if (ensure_events(c, size_t(2 * nc + 1))) return -1;
+    const size_t img_elems = size_t(3) * kImage * kImage, out_elems = size_t(kDim) * kTokens;
+    cudaEvent_t start = c->events[2 * nc];
+    S3T_CUDA(cudaEventRecord(start, st));   // earlier work on st may still use the buffers
+    S3T_CUDA(cudaStreamWaitEvent(c->copy_in, start, 0));
+    S3T_CUDA(cudaStreamWaitEvent(c->copy_out, start, 0));
+    for (int k = 0; k < nc; ++k) {
+        const int b0 = k * kHostChunk, nb = std::min(kHostChunk, batch - b0);
+        S3T_CUDA(cudaMemcpyAsync(c->img + b0 * img_elems, images + b0 * img_elems, nb * img_elems * 4,
+                                 cudaMemcpyHostToDevice, c->copy_in));
+        S3T_CUDA(cudaEventRecord(c->events[k], c->copy_in));
+    }
+    for (int k = 0; k < nc; ++k) {
+        const int b0 = k * kHostChunk, nb = std::min(kHostChunk, batch - b0);
+        cudaGraphExec_t g = nullptr;
+        if (trunk_graph(c, c->img + b0 * img_elems, nb, n_layers, c->out + b0 * out_elems, &g)) return -1;
+        S3T_CUDA(cudaStreamWaitEvent(st, c->events[k], 0));
+        S3T_CUDA(cudaGraphLaunch(g, st));
+        S3T_CUDA(cudaEventRecord(c->events[nc + k], st));
+        S3T_CUDA(cudaStreamWaitEvent(c->copy_out, c->events[nc + k], 0));
+        S3T_CUDA(cudaMemcpyAsync(out + b0 * out_elems, c->out + b0 * out_elems, nb * out_elems * 4,
+                                 cudaMemcpyDeviceToHost, c->copy_out));
+    }
+    S3T_CUDA(cudaEventRecord(start, c->copy_out));
+    S3T_CUDA(cudaStreamWaitEvent(st, start, 0));
+    return check_status(c, st);
+}
+
+int run_impl(s3t_ctx* c, const float* images, int batch, int n_layers, float* out, int flags, void* stream) {
+    if (!c) return fail("ctx is null");
+    if (!c->finalized) return fail("weights not finalized (call s3t_finalize_weights)");
+    if (!images || !out) return fail("images or out is null");
+    if (batch <= 0) return fail("batch must be positive");
+    if (n_layers < 0 || n_layers > c->n_layers) return fail("n_layers out of range");
+    S3T_CUDA(cudaSetDevice(c->device));
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+    if (ensure_workspace(c, batch)) return -1;
+
+    const bool in_dev = flags & S3T_IMAGES_ON_DEVICE, out_dev = flags & S3T_OUTPUT_ON_DEVICE;
+    if (!in_dev && !out_dev && n_layers > 0 && batch > kHostChunk)
+        return run_host_pipelined(c, images, batch, n_layers, out, st);
+
+    const size_t in_bytes = size_t(batch) * 3 * kImage * kImage * 4;
+    const size_t out_bytes = size_t(batch) * kDim * kTokens * 4;
+    const float* din = in_dev ? images : c->img;
+    float* dout = out_dev ? out : c->out;
+    if (!in_dev) S3T_CUDA(cudaMemcpyAsync(c->img, images, in_bytes, cudaMemcpyHostToDevice, st));
+
+    if (n_layers == 0) {
+        if (run_stem(c, din, batch, out, out_dev, st)) return -1;
+        return check_status(c, st);
+    }
+
+    cudaGraphExec_t g = nullptr;
+    if (trunk_graph(c, din, batch, n_layers, dout, &g)) return -1;
+    S3T_CUDA(cudaGraphLaunch(g, st));
     if (!out_dev) {
         S3T_CUDA(cudaMemcpyAsync(out, c->out, out_bytes, cudaMemcpyDeviceToHost, st));
         return check_status(c, st);
@@ -551,6 +614,9 @@ void s3t_destroy(s3t_ctx* c) {
     for (auto& kv : c->staged)
         if (kv.second.dev) cudaFree(kv.second.dev);
     for (void* p : c->allocs) cudaFree(p);
+    for (cudaEvent_t e : c->events) cudaEventDestroy(e);
+    if (c->copy_in) cudaStreamDestroy(c->copy_in);
+    if (c->copy_out) cudaStreamDestroy(c->copy_out);
     cudaStreamDestroy(c->stream);
     delete c;
 }

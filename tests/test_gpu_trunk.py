@@ -90,6 +90,20 @@ def test_batch_matches_single(gpu):
         assert np.array_equal(batched[i], single[0])
 
 
+def test_host_pipelined_batch_matches_single(gpu):
+    """A host-buffer batch larger than one pipeline chunk (10 = 8 + 2 images)
+    is uploaded, computed and downloaded in overlapping chunks; every image
+    must equal its own batch-1 run."""
+    from sam3cpp_b200 import synthetic as s
+    path, _ = _models("f16", 2, True)
+    trunk = gpu.VisionTrunk(gpu.GgufModel(path))
+    imgs = s.synthetic_images(10)
+    batched = trunk.run_batch(imgs)
+    for i in (0, 7, 8, 9):
+        single = trunk.run_batch(imgs[i:i + 1])
+        assert np.array_equal(batched[i], single[0]), i
+
+
 def test_reference_errors(gpu):
     """Shape and payload errors follow src/vision_trunk.cpp:301-306."""
     from sam3cpp_b200 import synthetic as s
