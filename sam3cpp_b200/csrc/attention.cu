@@ -170,32 +170,43 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
             const int my_items = int(blockIdx.x) < n_items ? (n_items - 1 - int(blockIdx.x)) / int(gridDim.x) + 1 : 0;
             const int total = my_items * nkv;
             bool ok = true, issued = false;
-            // S for this CTA's global block b (item b / nkv, key block b % nkv)
-            auto issue_s = [&](int b) -> bool {
-                const int li = b / nkv, j = b - li * nkv, s = b % kKVStages;
-                const int qb = li & 1;
-                if (j == 0 && !mbar_wait(q_full + qb, (li >> 1) & 1, a.status, kErrTimeoutMma, abort_flag))
+            // Descriptors are built once; a K step of 16 advances the start
+            // address field by 32 bytes (2) for K-major tiles and by 16 rows
+            // of 128 bytes (128) for the MN-major V tile.
+            const uint64_t dQ0 = umma_desc_sw128(smem_u32(sQ), 16, 1024);
+            const uint64_t dQ1 = umma_desc_sw128(smem_u32(sQ + kQBytes), 16, 1024);
+            const uint64_t dK0 = umma_desc_sw128(smem_u32(sK), 16, 1024);
+            const uint64_t dV0 = umma_desc_sw128(smem_u32(sV), kKVBytes, 1024);
+            const uint64_t dP = umma_desc_sw128(smem_u32(sP), 16, 1024);
+            constexpr uint64_t kStageStep = kKVBytes >> 4;
+            // State of the next S block to issue (block counter, key block, item, ring stage/phase).
+            int sb = 0, sj = 0, sli = 0, ss = 0;
+            uint32_t sph = 0;
+            auto issue_s = [&]() -> bool {
+                const int qb = sli & 1;
+                if (sj == 0 && !mbar_wait(q_full + qb, (sli >> 1) & 1, a.status, kErrTimeoutMma, abort_flag))
                     return false;
-                if (!mbar_wait(kv_full + s, (b / kKVStages) & 1, a.status, kErrTimeoutMma, abort_flag)) return false;
-                if (b > 0 && !mbar_wait(s_free, (b - 1) & 1, a.status, kErrTimeoutMma, abort_flag)) return false;
+                if (!mbar_wait(kv_full + ss, sph, a.status, kErrTimeoutMma, abort_flag)) return false;
+                if (sb > 0 && !mbar_wait(s_free, (sb - 1) & 1, a.status, kErrTimeoutMma, abort_flag)) return false;
                 tc_fence_after();
-                const uint32_t q0 = smem_u32(sQ + qb * kQBytes), k0 = smem_u32(sK + s * kKVBytes);
+                const uint64_t dq = qb ? dQ1 : dQ0, dk = dK0 + uint64_t(ss) * kStageStep;
 #pragma unroll
-                for (int k = 0; k < kD / 16; ++k)
-                    umma_f16_ss(tS, umma_desc_sw128(q0 + k * 32, 16, 1024), umma_desc_sw128(k0 + k * 32, 16, 1024),
-                                idS, k != 0);
+                for (int k = 0; k < kD / 16; ++k) umma_f16_ss(tS, dq + 2 * k, dk + 2 * k, idS, k != 0);
                 umma_commit(s_full);
-                if (j == nkv - 1) umma_commit(q_empty + qb);   // Q buffer reusable once these S complete
+                if (sj == nkv - 1) umma_commit(q_empty + qb);   // Q buffer reusable once these S complete
                 issued = true;
+                ++sb;
+                if (++sj == nkv) { sj = 0; ++sli; }
+                if (++ss == kKVStages) { ss = 0; sph ^= 1; }
                 return true;
             };
-            if (total > 0) ok = issue_s(0);
+            if (total > 0) ok = issue_s();
+            int j = 0, li = 0, s = 0;
             for (int b = 0; ok && b < total; ++b) {
-                if (b + 1 < total && !issue_s(b + 1)) {
+                if (b + 1 < total && !issue_s()) {
                     ok = false;
                     break;
                 }
-                const int li = b / nkv, j = b - li * nkv, s = b % kKVStages;
                 const int ob = li & 1;
                 if (!mbar_wait(p_full, b & 1, a.status, kErrTimeoutMma, abort_flag)) {
                     ok = false;
@@ -206,15 +217,14 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
                     break;
                 }
                 tc_fence_after();
-                const uint32_t v0 = smem_u32(sV + s * kKVBytes);
-                const uint32_t p0 = smem_u32(sP);
+                const uint64_t dv = dV0 + uint64_t(s) * kStageStep;
                 const uint32_t tO = tmem + 64 + ob * 64;
 #pragma unroll
-                for (int k = 0; k < kBKV / 16; ++k)
-                    umma_f16_ss(tO, umma_desc_sw128(p0 + k * 32, 16, 1024),
-                                umma_desc_sw128(v0 + k * 16 * 128, kKVBytes, 1024), idO, (j | k) != 0);
+                for (int k = 0; k < kBKV / 16; ++k) umma_f16_ss(tO, dP + 2 * k, dv + 128 * k, idO, (j | k) != 0);
                 umma_commit(kv_empty + s);
                 umma_commit(o_done + (b & 1));
+                if (++j == nkv) { j = 0; ++li; }
+                if (++s == kKVStages) s = 0;
             }
             if (!ok && issued) {
                 umma_commit(drain);

@@ -157,31 +157,34 @@ __global__ void f32_to_f16_kernel(const float* __restrict__ in, int64_t n, __hal
     if (i < n) out[i] = __float2half_rn(in[i]);
 }
 
-// Axial RoPE in place on [groups*16][L][64]; one thread per (row, 32-dim half).
+// Axial RoPE in place on [groups*16][L][64]; one thread per (row, 8-dim
+// slice): one 16-byte load and store, cos/sin as float4 loads.  Row counts
+// fit in 32 bits (<= 64 images x 9 x 16 x 576).
 template <typename T>
 __global__ void rope_kernel(T* x, int groups, int L, int windowed, const float* rl, const float* rg) {
-    const int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-    const int64_t total = int64_t(groups) * kHeads * L * 2;
+    const uint32_t idx = blockIdx.x * blockDim.x + threadIdx.x;
+    const uint32_t total = uint32_t(groups) * kHeads * L * 8;
     if (idx >= total) return;
-    const int half = int(idx & 1);
-    const int64_t r = idx >> 1;
-    const int i = int(r % L);
-    int px, py;
-    const float* tab;
-    if (windowed) {
-        py = i / kWindow; px = i % kWindow; tab = rl;
-    } else {
-        py = i / kGrid; px = i % kGrid; tab = rg;
-    }
-    const float* cs = tab + (half ? py : px) * 32;
-    T* v = x + r * kHeadDim + half * 32;
+    const uint32_t slice = idx & 7;          // dims 8*slice .. 8*slice+7
+    const uint32_t r = idx >> 3;
+    const uint32_t i = r % uint32_t(L);
+    const int half = slice >> 2;             // dims 0..31 -> x position, 32..63 -> y position
+    const int grid = windowed ? kWindow : kGrid;
+    const int pos = half ? int(i) / grid : int(i) % grid;
+    const float* cs = (windowed ? rl : rg) + pos * 32 + (slice & 3) * 4;   // pair index j = 4*(slice&3) + u
+    const float4 c4 = __ldg(reinterpret_cast<const float4*>(cs));
+    const float4 s4 = __ldg(reinterpret_cast<const float4*>(cs + 16));
+    const float c[4] = {c4.x, c4.y, c4.z, c4.w}, s[4] = {s4.x, s4.y, s4.z, s4.w};
+    uint4* p = reinterpret_cast<uint4*>(x + size_t(r) * kHeadDim + slice * 8);
+    uint4 u = *p;
+    T* v = reinterpret_cast<T*>(&u);
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-        const float c = cs[j], s = cs[16 + j];
+    for (int j = 0; j < 4; ++j) {
         const float x0 = float(v[2 * j]), x1 = float(v[2 * j + 1]);
-        v[2 * j] = T(x0 * c - x1 * s);
-        v[2 * j + 1] = T(x0 * s + x1 * c);
+        v[2 * j] = T(x0 * c[j] - x1 * s[j]);
+        v[2 * j + 1] = T(x0 * s[j] + x1 * c[j]);
     }
+    *p = u;
 }
 
 }  // namespace
@@ -226,7 +229,8 @@ cudaError_t launch_f32_to_f16(const float* in, int64_t n, __half* out, cudaStrea
 
 cudaError_t launch_rope_inplace(void* x, int groups, int L, int windowed, int bf16, const float* rl, const float* rg,
                                 cudaStream_t stream) {
-    const int64_t total = int64_t(groups) * kHeads * L * 2;
+    const int64_t total = int64_t(groups) * kHeads * L * 8;
+    if (total >= (int64_t(1) << 32)) return cudaErrorInvalidValue;
     const unsigned blocks = unsigned((total + 255) / 256);
     if (bf16)
         rope_kernel<__nv_bfloat16><<<blocks, 256, 0, stream>>>(static_cast<__nv_bfloat16*>(x), groups, L, windowed, rl, rg);
