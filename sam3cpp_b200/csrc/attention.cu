@@ -13,14 +13,18 @@
 // owner + UMMA issuer, warps 2..5 softmax + epilogue (one query row per
 // thread).  Per 64-key block b of an item:
 //   S = Q K^T   : UMMA M=128 N=64 K=64, accumulator in TMEM cols [0,64)
-//   P = 2^(S*scale*log2e - m) as fp16/bf16 into a 128-byte-swizzled smem tile
-//   O += P V    : UMMA M=128 N=64 K=64 (V MN-major) into TMEM O[item & 1]
+//   P = 2^(S*scale*log2e - m) as fp16/bf16 into TMEM P[b & 1] (32 columns)
+//   O += P V    : UMMA M=128 N=64 K=64, A = P read from TMEM, V MN-major from
+//                 shared memory, into TMEM O[item & 1]
 // The UMMA issuer runs one block ahead (S_{b+1} is issued as soon as S_b has
-// been read), across item boundaries too; Q and O are double-buffered so the
-// next item's loads and first S overlap the current item's epilogue.  The row
-// max used for P is raised only when a block exceeds it by more than 2^8 (O
-// is then rescaled in TMEM).  Shared memory (96 KB) and registers are sized
-// for two CTAs per SM; a 3-deep K/V ring keeps S_{b+1} from waiting on loads.
+// been read), across item boundaries too; P is double-buffered, so the
+// softmax of block b never waits for the PV of block b-1, and Q and O are
+// double-buffered so the next item's loads and first S overlap the current
+// item's epilogue.  P never touches shared memory (no proxy fence on the
+// critical path).  The row max used for P is raised only when a block
+// exceeds it by more than 2^8 (O is then rescaled in TMEM).  Shared memory
+// (80 KB) and registers are sized for two CTAs per SM; a 3-deep K/V ring
+// keeps S_{b+1} from waiting on loads.
 // L is a multiple of 64 for both layer kinds, so keys are never masked; query
 // rows past L (last tile of a group) are computed on zero-filled Q rows and
 // not stored.
@@ -34,9 +38,9 @@ namespace {
 constexpr int kBQ = 128, kBKV = 64, kD = 64, kKVStages = 3;
 constexpr uint32_t kQBytes = kBQ * kD * 2;      // 16 KB
 constexpr uint32_t kKVBytes = kBKV * kD * 2;    // 8 KB (each of K, V)
-constexpr uint32_t kPBytes = kBQ * kBKV * 2;    // 16 KB
-constexpr size_t kAttnSmem = 2 * kQBytes + 2 * kKVStages * kKVBytes + kPBytes + 1024 + 256;
-constexpr uint32_t kAttnTmemCols = 256;         // S [0,64), O0 [64,128), O1 [128,192)
+constexpr size_t kAttnSmem = 2 * kQBytes + 2 * kKVStages * kKVBytes + 1024 + 256;
+constexpr uint32_t kAttnTmemCols = 256;         // S [0,64), O0 [64,128), O1 [128,192), P0/P1 [192,256)
+constexpr uint32_t kTmemP = 192;                // P[x] at kTmemP + 32 x (64 fp16 keys per row)
 constexpr int kCtasPerSm = 2;
 
 template <int BF16>
@@ -67,16 +71,15 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
     uint8_t* sQ = smem;                              // 2 buffers
     uint8_t* sK = sQ + 2 * kQBytes;
     uint8_t* sV = sK + kKVStages * kKVBytes;
-    uint8_t* sP = sV + kKVStages * kKVBytes;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sP + kPBytes);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kKVStages * kKVBytes);
     uint64_t* q_full = bars;                         // [2]
     uint64_t* q_empty = q_full + 2;                  // [2]
     uint64_t* kv_full = q_empty + 2;                 // [S]
     uint64_t* kv_empty = kv_full + kKVStages;        // [S]
     uint64_t* s_full = kv_empty + kKVStages;
     uint64_t* s_free = s_full + 1;
-    uint64_t* p_full = s_free + 1;
-    uint64_t* o_done = p_full + 1;                   // [2]: PV of blocks with that parity
+    uint64_t* p_full = s_free + 1;                   // [2]: P of blocks with that parity
+    uint64_t* o_done = p_full + 2;                   // [2]: PV of blocks with that parity
     uint64_t* o_free = o_done + 2;                   // [2]
     uint64_t* drain = o_free + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -93,6 +96,7 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
             mbar_init(q_empty + i, 1);
             mbar_init(o_free + i, 4);
             mbar_init(o_done + i, 1);
+            mbar_init(p_full + i, 4);
         }
         for (int s = 0; s < kKVStages; ++s) {
             mbar_init(kv_full + s, 1);
@@ -100,7 +104,6 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
         }
         mbar_init(s_full, 1);
         mbar_init(s_free, 4);
-        mbar_init(p_full, 4);
         mbar_init(drain, 1);
         *abort_flag = 0;
         fence_barrier_init();
@@ -177,7 +180,6 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
             const uint64_t dQ1 = umma_desc_sw128(smem_u32(sQ + kQBytes), 16, 1024);
             const uint64_t dK0 = umma_desc_sw128(smem_u32(sK), 16, 1024);
             const uint64_t dV0 = umma_desc_sw128(smem_u32(sV), kKVBytes, 1024);
-            const uint64_t dP = umma_desc_sw128(smem_u32(sP), 16, 1024);
             constexpr uint64_t kStageStep = kKVBytes >> 4;
             // State of the next S block to issue (block counter, key block, item, ring stage/phase).
             int sb = 0, sj = 0, sli = 0, ss = 0;
@@ -208,7 +210,7 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
                     break;
                 }
                 const int ob = li & 1;
-                if (!mbar_wait(p_full, b & 1, a.status, kErrTimeoutMma, abort_flag)) {
+                if (!mbar_wait(p_full + (b & 1), (b >> 1) & 1, a.status, kErrTimeoutMma, abort_flag)) {
                     ok = false;
                     break;
                 }
@@ -219,8 +221,9 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
                 tc_fence_after();
                 const uint64_t dv = dV0 + uint64_t(s) * kStageStep;
                 const uint32_t tO = tmem + 64 + ob * 64;
+                const uint32_t tP = tmem + kTmemP + (b & 1) * 32;
 #pragma unroll
-                for (int k = 0; k < kBKV / 16; ++k) umma_f16_ss(tO, dP + 2 * k, dv + 128 * k, idO, (j | k) != 0);
+                for (int k = 0; k < kBKV / 16; ++k) umma_f16_ts(tO, tP + 8 * k, dv + 128 * k, idO, (j | k) != 0);
                 umma_commit(kv_empty + s);
                 umma_commit(o_done + (b & 1));
                 if (++j == nkv) { j = 0; ++li; }
@@ -287,9 +290,9 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
                 }
                 l_run = l_run * alpha + ((sums[0] + sums[1]) + (sums[2] + sums[3]));
 
-                // The P tile is free once the PV of block b-1 has completed.
-                if (b > 0) {
-                    if (!mbar_wait(o_done + ((b - 1) & 1), ((b - 1) >> 1) & 1, a.status, kErrTimeoutEpilogue, abort_flag)) {
+                // P buffer b & 1 is free once the PV of block b-2 has completed.
+                if (b > 1) {
+                    if (!mbar_wait(o_done + (b & 1), ((b - 2) >> 1) & 1, a.status, kErrTimeoutEpilogue, abort_flag)) {
                         ok = false;
                         break;
                     }
@@ -317,17 +320,12 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
                         tmem_wait_st();
                     }
                 }
-                // P row -> 128-byte swizzled smem row (16-byte chunk c at c ^ (row & 7)).
-                uint8_t* prow = sP + row * 128;
-#pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    uint4 u = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-                    *reinterpret_cast<uint4*>(prow + ((c ^ (row & 7)) << 4)) = u;
-                }
-                fence_proxy_async_smem();
+                // P row -> this row's TMEM lane (key 2i in the low half of column i).
+                tmem_st32(tmem + kTmemP + (b & 1) * 32 + lane_off, pk);
+                tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(p_full);
+                if (lane == 0) mbar_arrive(p_full + (b & 1));
                 m_run = m_new;
             }
             if (!ok || !mbar_wait(o_done + ((b - 1) & 1), ((b - 1) >> 1) & 1, a.status, kErrTimeoutEpilogue, abort_flag)) {
