@@ -60,6 +60,101 @@ __device__ __forceinline__ void store_half32(__half* dst, const float (&v)[32]) 
     }
 }
 
+// Bias, GELU and Q8_0 rounding of one 32-column chunk, packed to fp16 pairs.
+__device__ __forceinline__ void f16_chunk(const GemmArgs& a, int n, const uint32_t (&r)[32], uint32_t (&pk)[16]) {
+    float2 v[16];
+    if (a.bias) {
+        const float4* p = reinterpret_cast<const float4*>(a.bias + n);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float4 b = __ldg(p + i);
+            v[2 * i] = __fadd2_rn(make_float2(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1])),
+                                  make_float2(b.x, b.y));
+            v[2 * i + 1] = __fadd2_rn(make_float2(__uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3])),
+                                      make_float2(b.z, b.w));
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = make_float2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+    }
+    if (a.gelu) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = gelu_erf_as2(v[i]);
+    }
+    if (a.q8) {
+        float f[32];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) { f[2 * i] = v[i].x; f[2 * i + 1] = v[i].y; }
+        q8_0_fake_quant32(f);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = make_float2(f[2 * i], f[2 * i + 1]);
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) pk[i] = pack_half2(v[i].x, v[i].y);
+}
+
+// Token m of the QKV GEMM: its (window or image) group g and index i in that
+// group, and its RoPE row/column positions.
+struct QkvPos {
+    int g, i, px, py;
+};
+
+__device__ __forceinline__ QkvPos qkv_pos(int m, int windowed) {
+    const int img = m / kTokens, t = m - img * kTokens;
+    const int y = t / kGrid, x = t - y * kGrid;
+    QkvPos p;
+    if (windowed) {
+        p.g = img * 9 + (y / kWindow) * 3 + (x / kWindow);
+        p.py = y % kWindow;
+        p.px = x % kWindow;
+        p.i = p.py * kWindow + p.px;
+    } else {
+        p.g = img;
+        p.i = t;
+        p.px = x;
+        p.py = y;
+    }
+    return p;
+}
+
+// Bias and axial RoPE (q and k; columns n..n+31 are one half of a head) of one
+// 32-column chunk of row m, packed to fp16 pairs.
+__device__ __forceinline__ void qkv_chunk(const GemmArgs& a, int m, int n, const uint32_t (&r)[32],
+                                          uint32_t (&pk)[16]) {
+    float2 v[16];
+    {
+        const float4* p = reinterpret_cast<const float4*>(a.bias + n);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float4 b = __ldg(p + i);
+            v[2 * i] = __fadd2_rn(make_float2(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1])),
+                                  make_float2(b.x, b.y));
+            v[2 * i + 1] = __fadd2_rn(make_float2(__uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3])),
+                                      make_float2(b.z, b.w));
+        }
+    }
+    if ((n >> 10) < 2) {
+        const QkvPos p = qkv_pos(m, a.windowed);
+        const float* tab = a.windowed ? a.rope_local : a.rope_global;
+        const int half = (n >> 5) & 1;
+        const float4* cs = reinterpret_cast<const float4*>(tab + (half ? p.py : p.px) * 32);   // [pos][cos16 | sin16]
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const float4 c4 = __ldg(cs + q), s4 = __ldg(cs + 4 + q);
+            const float c[4] = {c4.x, c4.y, c4.z, c4.w}, s[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int j = 4 * q + u;
+                // (x0, x1) -> (x0 c - x1 s, x0 s + x1 c)
+                v[j] = __ffma2_rn(make_float2(v[j].x, v[j].x), make_float2(c[u], s[u]),
+                                  __fmul2_rn(make_float2(v[j].y, v[j].y), make_float2(-s[u], c[u])));
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) pk[i] = pack_half2(v[i].x, v[i].y);
+}
+
 template <int EPI>
 __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int m, int n, const uint32_t (&r)[32]) {
     float v[32];
@@ -316,28 +411,46 @@ __global__ void __launch_bounds__(192, 1)
 // barrier; the leader's commits arrive on both CTAs' barriers (multicast
 // commit); both CTAs' epilogue warps release an accumulator buffer on the
 // leader's barrier.  No TMA load uses cluster multicast.
+//
+// The epilogue warps sit on the same SM sub-partitions as the single
+// producer and UMMA threads, so every instruction they issue can delay the
+// mainloop: the UMMA loop uses descriptors built once, the fp32 epilogue
+// math runs as packed f32x2 operations (two columns per instruction), and the
+// plain fp16 output (kEpiF16) leaves through shared memory and one TMA store
+// per 32 x 32 chunk instead of 32 scattered row stores.
 struct PairCfg {
     static constexpr int BN = 256;
     static constexpr int STAGES = 6;
     static constexpr uint32_t A_BYTES = kBM * kBK * 2;          // this CTA's 128 rows of A
     static constexpr uint32_t B_BYTES = (BN / 2) * kBK * 2;     // this CTA's 128 rows of B
     static constexpr uint32_t TMEM_COLS = 2 * BN;
-    static constexpr size_t SMEM = size_t(STAGES) * (A_BYTES + B_BYTES) + 1024 + 256;
     static constexpr int EPI_WARPS = 8;
+    static constexpr int COL_GROUPS = EPI_WARPS / 4;            // warps per TMEM lane quarter
+    static constexpr int WARP_COLS = BN / COL_GROUPS;           // accumulator columns per warp
+    // kEpiF16 stages each 32x32 output chunk in shared memory (2 KB buffers,
+    // 64-byte swizzle) and stores it with TMA.
+    static constexpr int OUT_BUFS = EPI_WARPS <= 8 ? 2 : 1;
+    __host__ __device__ static constexpr bool staged_out(int EPI) { return EPI == kEpiF16 || EPI == kEpiQkv; }
+    static constexpr uint32_t OUT_BYTES = OUT_BUFS * 2048;
+    template <int EPI>
+    static constexpr size_t smem() {
+        return size_t(STAGES) * (A_BYTES + B_BYTES) + (staged_out(EPI) ? EPI_WARPS * OUT_BYTES : 0) + 1024 + 256;
+    }
     static constexpr int THREADS = 64 + 32 * EPI_WARPS;
 };
 
 template <int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg::THREADS, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     const GemmArgs args) {
+                     const __grid_constant__ CUtensorMap tmC, const GemmArgs args) {
     using Cfg = PairCfg;
     constexpr int STAGES = Cfg::STAGES, BN = Cfg::BN;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
     uint8_t* sB = smem + STAGES * Cfg::A_BYTES;
-    uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * Cfg::B_BYTES);
+    uint8_t* sOut = sB + STAGES * Cfg::B_BYTES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sOut + (Cfg::staged_out(EPI) ? Cfg::EPI_WARPS * Cfg::OUT_BYTES : 0));
     uint64_t* empty = full + STAGES;
     uint64_t* tfull = empty + STAGES;
     uint64_t* tempty = tfull + 2;
@@ -417,6 +530,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg::THREADS, 1)
     } else if (warp == 1) {
         if (lane == 0 && leader) {
             constexpr uint32_t idesc = umma_idesc_f16(2 * kBM, BN, 0, 0);
+            // Descriptors are built once; a stage advances the start address
+            // field by its byte size / 16, a K step of 16 by 32 bytes (2).
+            const uint64_t dA0 = umma_desc_sw128(smem_u32(sA), 16, 1024);
+            const uint64_t dB0 = umma_desc_sw128(smem_u32(sB), 16, 1024);
             int s = 0;
             uint32_t ph = 0;
             bool ok = true, issued = false;
@@ -436,12 +553,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg::THREADS, 1)
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a0 = smem_u32(sA + s * Cfg::A_BYTES);
-                    const uint32_t b0 = smem_u32(sB + s * Cfg::B_BYTES);
+                    const uint64_t da = dA0 + uint64_t(s) * (Cfg::A_BYTES >> 4);
+                    const uint64_t db = dB0 + uint64_t(s) * (Cfg::B_BYTES >> 4);
 #pragma unroll
                     for (int k = 0; k < kBK / 16; ++k)
-                        umma_f16_ss_pair(d_tmem, umma_desc_sw128(a0 + k * 32, 16, 1024),
-                                         umma_desc_sw128(b0 + k * 32, 16, 1024), idesc, (kb | k) != 0);
+                        umma_f16_ss_pair(d_tmem, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0);
                     issued = true;
                     umma_commit_pair(empty + s, 0x3);
                     if (++s == STAGES) {
@@ -458,42 +574,119 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg::THREADS, 1)
             }
         }
     } else {
-        // Epilogue warps 2..9: warp w reads TMEM lane quarter w % 4 (rows
-        // 32*(w%4)..+31 of this CTA's half) and half of the 256 columns.
+        // Epilogue warps 2..EPI_WARPS+1: warp w reads TMEM lane quarter w % 4
+        // (rows 32*(w%4)..+31 of this CTA's half) and WARP_COLS of the 256 columns.
         const int quarter = warp & 3;
-        const int col_half = (warp - 2) >> 2;
+        const int col_grp = (warp - 2) >> 2;
         const int row = quarter * 32 + lane;
         int local = 0;
         for (int tile = pair; tile < n_tiles; tile += n_pairs, ++local) {
             const int acc = local & 1;
             const uint32_t aph = (local >> 1) & 1;
             const int m = (tile / n_tiles_n) * 2 * kBM + int(rank) * kBM + row;
-            const int n0 = (tile % n_tiles_n) * BN + col_half * (BN / 2);
+            const int n0 = (tile % n_tiles_n) * BN + col_grp * Cfg::WARP_COLS;
             if constexpr (EPI == kEpiResid) {
                 // Pull this thread's residual slice (128 fp32 = 4 lines) into L2
                 // while the tile's mainloop is still running.
                 if (m < args.M) {
                     const float* xr = args.resid + int64_t(m) * args.N + n0;
 #pragma unroll
-                    for (int q = 0; q < 4; ++q)
+                    for (int q = 0; q < Cfg::WARP_COLS / 32; ++q)
                         if (n0 + 32 * q < args.N) prefetch_l2(xr + 32 * q);
                 }
             }
             if (!mbar_wait(tfull + acc, aph, args.status, kErrTimeoutEpilogue, abort_flag)) break;
             tc_fence_after();
-            const uint32_t tbase = tmem_base + (uint32_t(quarter * 32) << 16) + acc * BN + col_half * (BN / 2);
+            const uint32_t tbase = tmem_base + (uint32_t(quarter * 32) << 16) + acc * BN + col_grp * Cfg::WARP_COLS;
+            if constexpr (EPI == kEpiF16) {
+                // Rows row0..row0+31 of the chunk go out through shared memory
+                // and one TMA store per warp (rows past M are not written).
+                uint8_t* stage = sOut + (warp - 2) * Cfg::OUT_BYTES;
+                const int row0 = m - lane;
 #pragma unroll 1
-            for (int c = 0; c < BN / 64; ++c) {
-                const int n = n0 + c * 32;
-                if (n >= args.N) break;
-                uint32_t r[32];
-                tmem_ld32(tbase + c * 32, r);
-                tmem_wait_ld();
-                if (m < args.M) epilogue_chunk<EPI>(args, m, n, r);
+                for (int c = 0; c < Cfg::WARP_COLS / 32; ++c) {
+                    const int n = n0 + c * 32;
+                    if (n >= args.N) break;
+                    uint32_t r[32];
+                    tmem_ld32(tbase + c * 32, r);
+                    tmem_wait_ld();
+                    uint32_t pk[16];
+                    f16_chunk(args, n, r, pk);
+                    uint8_t* buf = stage + (c % Cfg::OUT_BUFS) * 2048;
+                    if (lane == 0) bulk_wait_group_read<Cfg::OUT_BUFS - 1>();   // earlier store has read buf
+                    __syncwarp();
+                    uint8_t* rowp = buf + lane * 64;
+                    const int sw = (lane >> 1) & 3;
+#pragma unroll
+                    for (int q = 0; q < 4; ++q)
+                        *reinterpret_cast<uint4*>(rowp + ((q ^ sw) << 4)) =
+                            make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        if (row0 < args.M) tma_store_2d(&tmC, buf, n, row0);
+                        bulk_commit_group();
+                    }
+                }
+            } else if constexpr (EPI == kEpiQkv) {
+                // As above, but a 32-row chunk is stored as four 8-row boxes
+                // into the [which][group][head][token][64] layout: 8 tokens in
+                // a row of the grid never straddle a window or an image.
+                uint8_t* stage = sOut + (warp - 2) * Cfg::OUT_BYTES;
+                const int row0 = m - lane;
+                const int L = args.windowed ? kWindow * kWindow : kTokens;
+                const int planes = int(args.qkv_stride / (int64_t(L) * kHeadDim));   // group x head planes per q/k/v
+#pragma unroll 1
+                for (int c = 0; c < Cfg::WARP_COLS / 32; ++c) {
+                    const int n = n0 + c * 32;
+                    if (n >= args.N) break;
+                    uint32_t r[32];
+                    tmem_ld32(tbase + c * 32, r);
+                    tmem_wait_ld();
+                    uint32_t pk[16];
+                    qkv_chunk(args, m, n, r, pk);
+                    uint8_t* buf = stage + (c % Cfg::OUT_BUFS) * 2048;
+                    if (lane == 0) bulk_wait_group_read<Cfg::OUT_BUFS - 1>();
+                    __syncwarp();
+                    uint8_t* rowp = buf + lane * 64;
+                    const int sw = (lane >> 1) & 3;
+#pragma unroll
+                    for (int q = 0; q < 4; ++q)
+                        *reinterpret_cast<uint4*>(rowp + ((q ^ sw) << 4)) =
+                            make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        const int which = n >> 10, head = (n & 1023) >> 6, half = (n >> 5) & 1;
+#pragma unroll
+                        for (int r8 = 0; r8 < 4; ++r8) {
+                            const int mm = row0 + 8 * r8;
+                            if (mm < args.M) {
+                                const QkvPos p = qkv_pos(mm, args.windowed);
+                                tma_store_3d(&tmC, buf + r8 * 512, half * 32, p.i,
+                                             which * planes + p.g * kHeads + head);
+                            }
+                        }
+                        bulk_commit_group();
+                    }
+                }
+            } else {
+#pragma unroll 1
+                for (int c = 0; c < Cfg::WARP_COLS / 32; ++c) {
+                    const int n = n0 + c * 32;
+                    if (n >= args.N) break;
+                    uint32_t r[32];
+                    tmem_ld32(tbase + c * 32, r);
+                    tmem_wait_ld();
+                    if (m < args.M) epilogue_chunk<EPI>(args, m, n, r);
+                }
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(tempty + acc), 0));
+        }
+        if constexpr (Cfg::staged_out(EPI)) {
+            if (lane == 0) bulk_wait_group_all();
         }
     }
 
@@ -548,13 +741,27 @@ cudaError_t launch_pair(const __half* A, const __half* B, const GemmArgs& args, 
     // Persistent grid: only as many pairs as can be resident at once.
     const int max_pairs = g_pair_capacity > 0 ? g_pair_capacity : num_sms / 2;
     const int pairs = n_tiles < max_pairs ? n_tiles : max_pairs;
-    gemm_pair_kernel<EPI><<<2 * pairs, PairCfg::THREADS, PairCfg::SMEM, stream>>>(ta, tb, args);
+    CUtensorMap tc = ta;
+    if (EPI == kEpiF16 &&
+        !make_tmap_2d(&tc, args.out16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, args.N, args.M, 32, 32,
+                      CU_TENSOR_MAP_SWIZZLE_64B))
+        return cudaErrorInvalidValue;
+    if (EPI == kEpiQkv) {
+        // q, k, v: qkv_stride elements each, contiguous; one plane per (group, head).
+        const uint64_t L = args.windowed ? kWindow * kWindow : kTokens;
+        if (args.N != 3 * kDim || args.qkv_stride % int64_t(L * kHeadDim) != 0 ||
+            !make_tmap_3d(&tc, args.qkv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, kHeadDim, L,
+                          3 * uint64_t(args.qkv_stride) / (L * kHeadDim), 32, 8, CU_TENSOR_MAP_SWIZZLE_64B))
+            return cudaErrorInvalidValue;
+    }
+    gemm_pair_kernel<EPI><<<2 * pairs, PairCfg::THREADS, PairCfg::smem<EPI>(), stream>>>(ta, tb, tc, args);
     return cudaGetLastError();
 }
 
 template <int EPI>
 cudaError_t prepare_pair() {
-    return cudaFuncSetAttribute(gemm_pair_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(PairCfg::SMEM));
+    return cudaFuncSetAttribute(gemm_pair_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(PairCfg::smem<EPI>()));
 }
 
 template <int BN, int EPI>
@@ -581,7 +788,7 @@ cudaError_t gemm_prepare() {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(sms, 1, 1);
         cfg.blockDim = dim3(PairCfg::THREADS, 1, 1);
-        cfg.dynamicSmemBytes = PairCfg::SMEM;
+        cfg.dynamicSmemBytes = PairCfg::smem<kEpiF16>();
         cudaLaunchAttribute attr;
         attr.id = cudaLaunchAttributeClusterDimension;
         attr.val.clusterDim.x = 2;
@@ -600,7 +807,7 @@ cudaError_t gemm_prepare() {
 }
 
 bool make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,
-                  uint64_t outer, uint32_t box_inner, uint32_t box_outer) {
+                  uint64_t outer, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return false;
     cuuint64_t dims[2] = {inner, outer};
@@ -608,12 +815,12 @@ bool make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, in
     cuuint32_t box[2] = {box_inner, box_outer};
     cuuint32_t estr[2] = {1, 1};
     return fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 bool make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t d0,
-                  uint64_t d1, uint64_t d2, uint32_t b0, uint32_t b1) {
+                  uint64_t d1, uint64_t d2, uint32_t b0, uint32_t b1, CUtensorMapSwizzle swizzle) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return false;
     cuuint64_t dims[3] = {d0, d1, d2};
@@ -621,7 +828,7 @@ bool make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, in
     cuuint32_t box[3] = {b0, b1, 1};
     cuuint32_t estr[3] = {1, 1, 1};
     return fn(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 

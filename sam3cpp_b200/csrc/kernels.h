@@ -109,9 +109,11 @@ struct StemView {
 
 // Tensor-map creation through the driver entry point.
 bool make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,
-                  uint64_t outer, uint32_t box_inner, uint32_t box_outer);
+                  uint64_t outer, uint32_t box_inner, uint32_t box_outer,
+                  CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B);
 bool make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t d0,
-                  uint64_t d1, uint64_t d2, uint32_t b0, uint32_t b1);
+                  uint64_t d1, uint64_t d2, uint32_t b0, uint32_t b1,
+                  CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B);
 
 }  // namespace s3t
 

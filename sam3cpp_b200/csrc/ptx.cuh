@@ -145,6 +145,31 @@ S3T_DEV void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t leader
 }
 
 // Make generic-proxy shared-memory writes visible to the async proxy (UMMA).
+// Tiled bulk store shared -> global (bulk-group completion).  Rows or
+// columns of the box outside the tensor are not written.
+S3T_DEV void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map),
+                 "r"(smem_u32(src)), "r"(x), "r"(y)
+                 : "memory");
+}
+
+S3T_DEV void tma_store_3d(const CUtensorMap* map, const void* src, int x, int y, int z) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(map),
+                 "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
+                 : "memory");
+}
+
+S3T_DEV void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+
+// Wait until at most N bulk groups of this thread still read shared memory.
+template <int N>
+S3T_DEV void bulk_wait_group_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+// Wait until every bulk group of this thread has completed.
+S3T_DEV void bulk_wait_group_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 S3T_DEV void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -352,15 +377,34 @@ S3T_DEV float exp2_poly(float x) {
 // erf(z) = 1 - (a1 t + ... + a5 t^5) exp(-z^2), t = 1/(1 + p z), z >= 0.
 // Same function as ggml_vec_gelu_erf_f32: 0.5 x (1 + erf(x / sqrt 2)).
 S3T_DEV float gelu_erf_as(float x) {
-    const float z = fabsf(x) * 0.70710678118654752f;
-    const float t = rcp_approx(fmaf(0.3275911f, z, 1.0f));
-    float q = fmaf(1.061405429f, t, -1.453152027f);
-    q = fmaf(q, t, 1.421413741f);
-    q = fmaf(q, t, -0.284496736f);
-    q = fmaf(q, t, 0.254829592f);
-    q = q * t * ex2_approx(-z * z * 1.44269504088896341f);   // poly(t) * exp(-z^2)
-    const float one_plus_erf = x >= 0.f ? 2.0f - q : q;
-    return 0.5f * x * one_plus_erf;
+    // GELU(x) = relu(x) - |x| Q(x), Q = erfc(|x| / sqrt 2) / 2 = 0.5 poly(t) t exp(-x^2 / 2)
+    const float ax = fabsf(x);
+    const float t = rcp_approx(fmaf(0.3275911f * 0.70710678118654752f, ax, 1.0f));
+    float q = fmaf(0.5f * 1.061405429f, t, 0.5f * -1.453152027f);
+    q = fmaf(q, t, 0.5f * 1.421413741f);
+    q = fmaf(q, t, 0.5f * -0.284496736f);
+    q = fmaf(q, t, 0.5f * 0.254829592f);
+    const float e = ex2_approx(x * x * -0.72134752044448170f);   // exp(-x^2 / 2)
+    return fmaf(-(ax * t) * q, e, fmaxf(x, 0.f));
+}
+
+// Two lanes of gelu_erf_as with packed f32x2 arithmetic (same operations,
+// round-to-nearest, so each lane's result equals the scalar one).
+S3T_DEV float2 gelu_erf_as2(float2 x) {
+    const float2 ax = make_float2(fabsf(x.x), fabsf(x.y));
+    const float2 d = __ffma2_rn(make_float2(0.3275911f * 0.70710678118654752f, 0.3275911f * 0.70710678118654752f), ax,
+                                make_float2(1.0f, 1.0f));
+    const float2 t = make_float2(rcp_approx(d.x), rcp_approx(d.y));
+    // -Q(x) / (|x| t exp(-x^2/2)) as a polynomial in t (coefficients negated).
+    float2 q = __ffma2_rn(make_float2(-0.5f * 1.061405429f, -0.5f * 1.061405429f), t,
+                          make_float2(0.5f * 1.453152027f, 0.5f * 1.453152027f));
+    q = __ffma2_rn(q, t, make_float2(-0.5f * 1.421413741f, -0.5f * 1.421413741f));
+    q = __ffma2_rn(q, t, make_float2(0.5f * 0.284496736f, 0.5f * 0.284496736f));
+    q = __ffma2_rn(q, t, make_float2(-0.5f * 0.254829592f, -0.5f * 0.254829592f));
+    const float2 s = __fmul2_rn(__fmul2_rn(x, x), make_float2(-0.72134752044448170f, -0.72134752044448170f));
+    const float2 e = make_float2(ex2_approx(s.x), ex2_approx(s.y));
+    const float2 u = __fmul2_rn(__fmul2_rn(ax, t), q);
+    return __ffma2_rn(u, e, make_float2(fmaxf(x.x, 0.f), fmaxf(x.y, 0.f)));
 }
 
 S3T_DEV uint32_t pack_half2(float a, float b) {
