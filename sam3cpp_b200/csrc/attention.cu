@@ -279,16 +279,19 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
                 const bool raise = mx > m_run + kRescaleSlack;
                 const float m_new = raise ? mx : m_run;
                 const float alpha = raise ? ex2_approx(m_run - m_new) : 1.0f;
+                // Two scores per packed f32x2 instruction (fewer issue slots).
                 uint32_t pk[32];
-                float sums[4] = {0.f, 0.f, 0.f, 0.f};
+                float2 sums[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+                const float2 sl2x2 = make_float2(sl2, sl2), negm = make_float2(-m_new, -m_new);
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
-                    const float e0 = ex2_approx(fmaf(__uint_as_float(r[2 * i]), sl2, -m_new));
-                    const float e1 = ex2_approx(fmaf(__uint_as_float(r[2 * i + 1]), sl2, -m_new));
-                    sums[i & 3] += e0 + e1;
-                    pk[i] = pack2<BF16>(e0, e1);
+                    const float2 t = __ffma2_rn(make_float2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])),
+                                                sl2x2, negm);
+                    const float2 e = make_float2(ex2_approx(t.x), ex2_approx(t.y));
+                    sums[i & 1] = __fadd2_rn(sums[i & 1], e);
+                    pk[i] = pack2<BF16>(e.x, e.y);
                 }
-                l_run = l_run * alpha + ((sums[0] + sums[1]) + (sums[2] + sums[3]));
+                l_run = l_run * alpha + ((sums[0].x + sums[1].x) + (sums[0].y + sums[1].y));
 
                 // P buffer b & 1 is free once the PV of block b-2 has completed.
                 if (b > 1) {
