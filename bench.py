@@ -384,7 +384,30 @@ def config_extras(torch, dev, stream, trunk, syn, s3t):
     except Exception as e:  # reported, not fatal for the headline line
         res["q8_0_b8_error"] = str(e)
     res["attention_microbench_bf16"] = attention_microbench(torch, dev, stream)
+    res["rgb8"] = rgb8_extras(torch, dev, stream, trunk, s3t)
     return res
+
+
+def rgb8_extras(torch, dev, stream, trunk, s3t, batch=8, height=1080, width=1920):
+    """Decoded 8-bit frames (1920x1080, seeded uniform bytes) through the
+    reference's load_image_rgb preprocessing on the device: the preprocess
+    kernel alone (device in/out) and the whole uint8-in -> features-out run."""
+    import numpy as np
+    rgb_host = torch.from_numpy(np.random.default_rng(3).integers(0, 256, (batch, height, width, 3),
+                                                                  dtype=np.uint8)).pin_memory()
+    rgb = rgb_host.to(dev)
+    img = torch.empty((batch, 3, 1008, 1008), device=dev)
+    out = torch.empty((batch, 1024, 72, 72), device=dev)
+    pre = lambda: s3t.preprocess_rgb8(dev.index, rgb.data_ptr(), width, height, batch, img.data_ptr(),
+                                      stream.cuda_stream)
+    ms_pre = _event_ms(torch, dev, stream, pre, 3, 20)
+    run = lambda: trunk.run_rgb8_device(rgb.data_ptr(), width, height, batch, out.data_ptr(), stream.cuda_stream)
+    ms_run = _event_ms(torch, dev, stream, run, 2, 5)
+    trunk.sync(stream.cuda_stream)
+    written = batch * 3 * 1008 * 1008 * 4
+    return {"frame": f"{width}x{height} uint8 RGB", "batch": batch,
+            "preprocess_ms": round(ms_pre, 4), "preprocess_gbs": round(written / (ms_pre / 1e3) / 1e9, 1),
+            "trunk_from_rgb8_images_per_s": round(batch / (ms_run / 1e3), 2)}
 
 
 def cpu_baseline(fmt):

@@ -75,6 +75,18 @@ int s3t_trunk_run(s3t_ctx *ctx, const float *images_nchw, int batch, float *out_
 int s3t_trunk_run_layers(s3t_ctx *ctx, const float *images_nchw, int batch, int n_layers, float *out_nchw, int flags,
                          void *stream);
 
+/* The trunk from decoded 8-bit RGB: rgb [batch][height][width][3] uint8
+ * (row-major HWC, what stbi_load returns; all images of a call share one
+ * size) is resized and normalized on the device exactly as the reference's
+ * load_image_rgb (src/pipeline.cpp:45-83; tools/sam3_vision_trunk.cpp:33-66
+ * bilinear_resize_rgb) and then run through the trunk, replacing the host
+ * preprocessing loop and the 12 MB fp32 image per request.  flags as for
+ * s3t_trunk_run: S3T_IMAGES_ON_DEVICE means rgb is a device pointer.
+ * 1 <= width, height <= 32768.  Image decoding (stbi_load) stays with the
+ * caller. */
+int s3t_trunk_run_rgb8(s3t_ctx *ctx, const uint8_t *rgb, int width, int height, int batch, float *out_nchw,
+                       int flags, void *stream);
+
 /* Wait for the context's queued work and report any device-side error. */
 int s3t_sync(s3t_ctx *ctx, void *stream);
 
@@ -95,6 +107,13 @@ int s3t_gemm_f16(int device, const void *x16, const void *w16, const float *bias
  * order (windowed: 9 groups per image).  Device pointers. */
 int s3t_attention(int device, const void *q, const void *k, const void *v, int groups, int L, int windowed, int bf16,
                   void *out, void *stream);
+
+/* The preprocessing of s3t_trunk_run_rgb8 alone: rgb_dev [batch][height]
+ * [width][3] uint8 -> out_dev [batch][3][1008][1008] fp32, bit-exact with
+ * the reference's bilinear_resize_rgb (tools/sam3_vision_trunk.cpp:33-66).
+ * Device pointers on `device`, enqueued on `stream`. */
+int s3t_preprocess_rgb8(int device, const uint8_t *rgb_dev, int width, int height, int batch, float *out_dev,
+                        void *stream);
 
 /* Axial RoPE in place on grouped q or k (layout as above). */
 int s3t_rope(int device, void *x, int groups, int L, int windowed, int bf16, void *stream);

@@ -48,6 +48,7 @@ class Oracle:
         L.or_patch_embed.argtypes = [C.c_int, _p, _p, _p]
         L.or_trunk_run.argtypes = [_p, _p, C.c_int, _p, _p]
         L.or_set_sum_variant.argtypes = [C.c_int]
+        L.or_bilinear_resize_rgb.argtypes = [_p, C.c_int, C.c_int, _p]
 
     def set_sum_variant(self, v: int):
         self.lib.or_set_sum_variant(v)
@@ -120,6 +121,14 @@ class Oracle:
         y = np.empty_like(x)
         self.lib.or_gelu_erf(_ptr(x), x.size, _ptr(y))
         return y
+
+    def bilinear_resize_rgb(self, rgb):
+        """uint8 [h, w, 3] -> [3, 1008, 1008] fp32 (tools/sam3_vision_trunk.cpp:33-66)."""
+        src = np.ascontiguousarray(rgb, np.uint8)
+        h, w = src.shape[:2]
+        out = np.empty((3, 1008, 1008), np.float32)
+        self.lib.or_bilinear_resize_rgb(_ptr(src), w, h, _ptr(out))
+        return out
 
     def patch_embed(self, wtype, w_raw, image):
         img = np.ascontiguousarray(image, np.float32).reshape(3, 1008, 1008)
@@ -256,6 +265,7 @@ class Reference:
         L.ref_to_float.argtypes = [C.c_int, _p, _i64, _p]
         L.ref_fp32_to_fp16.argtypes = [_p, _i64, _p]
         L.ref_patch_embed.argtypes = [C.c_int, _p, _p, _p, C.c_int]
+        L.ref_bilinear_resize_rgb.argtypes = [_p, C.c_int, C.c_int, _p]
 
     def _check(self, rc):
         if rc != 0:
@@ -320,6 +330,13 @@ class Reference:
         y = np.empty(x.shape, np.uint16)
         self._check(self.lib.ref_fp32_to_fp16(_ptr(x), x.size, _ptr(y)))
         return y
+
+    def bilinear_resize_rgb(self, rgb):
+        src = np.ascontiguousarray(rgb, np.uint8)
+        h, w = src.shape[:2]
+        out = np.empty((3, 1008, 1008), np.float32)
+        self._check(self.lib.ref_bilinear_resize_rgb(_ptr(src), w, h, _ptr(out)))
+        return out
 
     def patch_embed(self, wtype, w_raw, image, n_threads=4):
         img = np.ascontiguousarray(image, np.float32)

@@ -463,3 +463,40 @@ int or_trunk_run(const or_trunk *t, const float *image, int n_run, float *out_to
     free(gq); free(gk); free(gv); free(go); free(px); free(py); free(idx);
     return 0;
 }
+
+/* Image preprocessing of tools/sam3_vision_trunk.cpp:33-66 (bilinear_resize_rgb;
+ * the same arithmetic as src/pipeline.cpp:45-83 load_image_rgb after stbi_load):
+ * uint8 RGB, row-major HWC -> [3][1008][1008] fp32, half-pixel-centre bilinear
+ * sampling with the source index clamped (the weight is taken from the clamped
+ * index, so it extrapolates at the top/left edge), p/255, then (v - 0.5)/0.5.
+ * Every product and sum is rounded on its own, as in the reference's scalar
+ * x86-64 build (no fused multiply-add). */
+__attribute__((optimize("fp-contract=off")))
+void or_bilinear_resize_rgb(const uint8_t *src, int w, int h, float *out) {
+    const int S = 1008;
+    const float xs = (float) w / (float) S, ys = (float) h / (float) S;
+    for (int dy = 0; dy < S; dy++) {
+        const float sy = ((float) dy + 0.5f) * ys - 0.5f;
+        int y0 = (int) floorf(sy);
+        y0 = y0 < 0 ? 0 : (y0 > h - 1 ? h - 1 : y0);
+        const int y1 = y0 + 1 > h - 1 ? h - 1 : y0 + 1;
+        const float wy = sy - (float) y0;
+        for (int dx = 0; dx < S; dx++) {
+            const float sx = ((float) dx + 0.5f) * xs - 0.5f;
+            int x0 = (int) floorf(sx);
+            x0 = x0 < 0 ? 0 : (x0 > w - 1 ? w - 1 : x0);
+            const int x1 = x0 + 1 > w - 1 ? w - 1 : x0 + 1;
+            const float wx = sx - (float) x0;
+            for (int c = 0; c < 3; c++) {
+                const float p00 = (float) src[((int64_t) y0 * w + x0) * 3 + c] / 255.0f;
+                const float p01 = (float) src[((int64_t) y0 * w + x1) * 3 + c] / 255.0f;
+                const float p10 = (float) src[((int64_t) y1 * w + x0) * 3 + c] / 255.0f;
+                const float p11 = (float) src[((int64_t) y1 * w + x1) * 3 + c] / 255.0f;
+                const float top = p00 + (p01 - p00) * wx;
+                const float bot = p10 + (p11 - p10) * wx;
+                const float v = top + (bot - top) * wy;
+                out[((int64_t) c * S + dy) * S + dx] = (v - 0.5f) / 0.5f;
+            }
+        }
+    }
+}

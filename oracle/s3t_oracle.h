@@ -38,6 +38,9 @@ void or_attention(const float *q, const float *k, const float *v, int64_t nq, in
                   int64_t heads, int64_t d, float scale, float *out);
 void or_gelu_erf(const float *x, int64_t n, float *y);
 void or_patch_embed(int wtype, const void *w, const float *image, float *out);
+/* uint8 RGB (h x w x 3) -> normalized [3][1008][1008] fp32, the reference's
+ * bilinear_resize_rgb (tools/sam3_vision_trunk.cpp:33-66). */
+void or_bilinear_resize_rgb(const uint8_t *src, int w, int h, float *out);
 
 typedef struct {
     int qkv_t, proj_t, fc1_t, fc2_t;

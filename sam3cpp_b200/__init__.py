@@ -65,6 +65,8 @@ def lib() -> C.CDLL:
         L.s3t_layernorm.argtypes = [i, p, i, p, p, p, i, p]
         L.s3t_device_status.argtypes = [i]
         L.s3t_stem_noalloc.argtypes = [p, p, i, p, p]
+        L.s3t_trunk_run_rgb8.argtypes = [p, p, i, i, i, p, i, p]
+        L.s3t_preprocess_rgb8.argtypes = [i, p, i, i, i, p, p]
         _lib = L
     return _lib
 
@@ -182,6 +184,27 @@ class VisionTrunk:
             check(L.s3t_trunk_run_layers(self.model.ctx, images.ctypes.data, b, n_layers, out.ctypes.data, 0, None))
         return out
 
+    def run_rgb8(self, rgb: np.ndarray) -> np.ndarray:
+        """Decoded 8-bit RGB [h, w, 3] or [B, h, w, 3] uint8 (stbi_load layout,
+        host) -> [B, 1024, 72, 72] fp32: the reference's load_image_rgb resize and
+        normalization (src/pipeline.cpp:45-83) on the device, then the trunk."""
+        rgb = np.ascontiguousarray(rgb, dtype=np.uint8)
+        if rgb.ndim == 3:
+            rgb = rgb[None]
+        if rgb.ndim != 4 or rgb.shape[3] != 3:
+            raise S3TError("rgb images must be uint8 [B, height, width, 3]")
+        b, h, w = rgb.shape[:3]
+        out = np.empty((b, DIM, GRID, GRID), np.float32)
+        check(lib().s3t_trunk_run_rgb8(self.model.ctx, rgb.ctypes.data, w, h, b, out.ctypes.data, 0, None))
+        return out
+
+    def run_rgb8_device(self, rgb_ptr: int, width: int, height: int, batch: int, out_ptr: int, stream: int = 0,
+                        rgb_on_device: bool = True, output_on_device: bool = True) -> None:
+        """Raw-pointer form of run_rgb8; enqueues on `stream`."""
+        flags = (IMAGES_ON_DEVICE if rgb_on_device else 0) | (OUTPUT_ON_DEVICE if output_on_device else 0)
+        check(lib().s3t_trunk_run_rgb8(self.model.ctx, C.c_void_p(rgb_ptr), width, height, batch,
+                                       C.c_void_p(out_ptr), flags, C.c_void_p(stream) if stream else None))
+
     def run_device(self, images_ptr: int, batch: int, out_ptr: int, stream: int = 0, images_on_device: bool = True,
                    output_on_device: bool = True) -> None:
         """Raw-pointer form (torch data_ptr()s); enqueues on `stream`."""
@@ -191,3 +214,11 @@ class VisionTrunk:
 
     def sync(self, stream: int = 0) -> None:
         check(lib().s3t_sync(self.model.ctx, C.c_void_p(stream) if stream else None))
+
+
+def preprocess_rgb8(device: int, rgb_ptr: int, width: int, height: int, batch: int, out_ptr: int,
+                    stream: int = 0) -> None:
+    """Device uint8 RGB [batch][height][width][3] -> device fp32 [batch][3][1008][1008],
+    the reference's bilinear_resize_rgb (tools/sam3_vision_trunk.cpp:33-66), bit-exact."""
+    check(lib().s3t_preprocess_rgb8(device, C.c_void_p(rgb_ptr), width, height, batch, C.c_void_p(out_ptr),
+                                    C.c_void_p(stream) if stream else None))

@@ -13,6 +13,7 @@ constexpr int kImage = 1008, kPatch = 14, kGrid = 72, kTokens = 5184, kDim = 102
 constexpr int kHeads = 16, kHeadDim = 64, kMlp = 4736, kLayers = 32, kWindow = 24;
 constexpr int kPatchK = 3 * 14 * 14;       // 588
 constexpr int kPatchKPad = 640;            // padded to the 64-wide K block
+constexpr int kMaxSourceSide = 32768;      // largest source image side the preprocessing accepts
 
 // Error codes written to the device status word (first writer wins).
 enum : int {
@@ -79,6 +80,9 @@ cudaError_t launch_layernorm_stem(float* x, int rows, const float* g0, const flo
 // ic*196 + kh*14 + kw, zero beyond 588.  round_f16: the pixel values become
 // fp16 (true for every weight format: the MMA operands are fp16).
 cudaError_t launch_im2col(const float* images, int batch, __half* cols, cudaStream_t stream);
+// uint8 RGB [batch][height][width][3] -> normalized [batch][3][1008][1008] fp32
+// (the reference's bilinear_resize_rgb, bit-exact).
+cudaError_t launch_resize_rgb8(const uint8_t* rgb, int width, int height, int batch, float* out, cudaStream_t stream);
 
 // Weight preparation (once per model).
 cudaError_t launch_dequant_q8_0_to_f16(const uint8_t* blocks, int64_t n, __half* out, cudaStream_t stream);

@@ -277,6 +277,8 @@ struct s3t_ctx {
     float* x = nullptr;
     __half *a16 = nullptr, *qkv = nullptr, *attn = nullptr, *h = nullptr, *cols = nullptr;
     float *img = nullptr, *out = nullptr;
+    uint8_t* rgb = nullptr;   // device copy of host uint8 images (s3t_trunk_run_rgb8)
+    size_t rgb_cap = 0;
 
     std::map<GraphKey, cudaGraphExec_t> graphs;
     cudaStream_t copy_in = nullptr, copy_out = nullptr;   // host-buffer pipelining
@@ -614,6 +616,7 @@ void s3t_destroy(s3t_ctx* c) {
     for (auto& kv : c->staged)
         if (kv.second.dev) cudaFree(kv.second.dev);
     for (void* p : c->allocs) cudaFree(p);
+    if (c->rgb) cudaFree(c->rgb);
     for (cudaEvent_t e : c->events) cudaEventDestroy(e);
     if (c->copy_in) cudaStreamDestroy(c->copy_in);
     if (c->copy_out) cudaStreamDestroy(c->copy_out);
@@ -825,6 +828,40 @@ int s3t_trunk_run_layers(s3t_ctx* c, const float* images, int batch, int n_layer
     return run_impl(c, images, batch, n_layers, out, flags, stream);
 }
 
+int s3t_trunk_run_rgb8(s3t_ctx* c, const uint8_t* rgb, int width, int height, int batch, float* out, int flags,
+                       void* stream) {
+    if (!c) return fail("ctx is null");
+    if (!c->finalized) return fail("weights not finalized (call s3t_finalize_weights)");
+    if (!rgb || !out) return fail("rgb or out is null");
+    if (batch <= 0 || batch > 65535) return fail("batch must be in [1, 65535]");
+    if (width <= 0 || height <= 0 || width > kMaxSourceSide || height > kMaxSourceSide)
+        return fail("image width and height must be in [1, 32768]");
+    S3T_CUDA(cudaSetDevice(c->device));
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+    if (ensure_workspace(c, batch)) return -1;
+    const uint8_t* src = rgb;
+    if (!(flags & S3T_IMAGES_ON_DEVICE)) {
+        const size_t bytes = size_t(batch) * size_t(height) * size_t(width) * 3;
+        if (bytes > c->rgb_cap) {
+            if (c->rgb) {
+                S3T_CUDA(cudaStreamSynchronize(st));
+                S3T_CUDA(cudaFree(c->rgb));
+                c->rgb = nullptr;
+                c->rgb_cap = 0;
+            }
+            void* q = nullptr;
+            const cudaError_t e = cudaMalloc(&q, bytes);
+            if (e != cudaSuccess) return fail("cudaMalloc(" + std::to_string(bytes) + "): " + cudaGetErrorString(e));
+            c->rgb = static_cast<uint8_t*>(q);
+            c->rgb_cap = bytes;
+        }
+        S3T_CUDA(cudaMemcpyAsync(c->rgb, rgb, bytes, cudaMemcpyHostToDevice, st));
+        src = c->rgb;
+    }
+    S3T_CUDA(launch_resize_rgb8(src, width, height, batch, c->img, st));
+    return run_impl(c, c->img, batch, c->n_layers, out, flags | S3T_IMAGES_ON_DEVICE, stream);
+}
+
 int s3t_sync(s3t_ctx* c, void* stream) {
     if (!c) return fail("ctx is null");
     S3T_CUDA(cudaSetDevice(c->device));
@@ -900,6 +937,18 @@ int s3t_layernorm(int device, const float* x, int rows, const float* gamma, cons
     if (device_state(device, &ds)) return -1;
     S3T_CUDA(cudaSetDevice(device));
     S3T_CUDA(launch_layernorm(x, rows, gamma, beta, static_cast<__half*>(y16), q8, static_cast<cudaStream_t>(stream)));
+    return 0;
+}
+
+int s3t_preprocess_rgb8(int device, const uint8_t* rgb, int width, int height, int batch, float* out, void* stream) {
+    DeviceState* ds = nullptr;
+    if (device_state(device, &ds)) return -1;
+    if (!rgb || !out) return fail("rgb or out is null");
+    if (batch <= 0 || batch > 65535) return fail("batch must be in [1, 65535]");
+    if (width <= 0 || height <= 0 || width > kMaxSourceSide || height > kMaxSourceSide)
+        return fail("image width and height must be in [1, 32768]");
+    S3T_CUDA(cudaSetDevice(device));
+    S3T_CUDA(launch_resize_rgb8(rgb, width, height, batch, out, static_cast<cudaStream_t>(stream)));
     return 0;
 }
 

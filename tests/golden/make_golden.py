@@ -7,11 +7,16 @@ sam3::VisionTrunk::run for the full-trunk outputs — on seeded inputs.
 
     python tests/golden/make_golden.py            # op vectors + all three trunks
     python tests/golden/make_golden.py --ops-only
+    python tests/golden/make_golden.py --preprocess-only
 
 Files:
   ops.npz                   inputs and ggml outputs of small op cases
   trunk_<fmt>_img0.npz      32-layer output on the seeded <fmt> file and image 0:
                             every STRIDE-th element, plus mean/std of all of it
+  preprocess.json           the reference tool's bilinear_resize_rgb
+                            (tools/sam3_vision_trunk.cpp:33-66) on seeded uint8
+                            images of PREPROCESS_SIZES: sha256 of the fp32
+                            output bytes and the values at PREPROCESS_PICKS
 """
 
 from __future__ import annotations
@@ -32,6 +37,35 @@ from oracle.pyoracle import F16, F32, Q8_0, Reference  # noqa: E402
 from sam3cpp_b200 import synthetic as s  # noqa: E402
 
 STRIDE = 61
+
+# (height, width) of the seeded uint8 RGB test images: identity size,
+# upsampling, downsampling, degenerate and odd sizes.  Image i is
+# default_rng(100 + i).integers(0, 256, (h, w, 3), dtype=uint8).
+PREPROCESS_SIZES = [(1008, 1008), (480, 640), (2000, 1500), (1, 1), (3, 7), (1009, 1007), (333, 2017)]
+
+
+def preprocess_image(i: int) -> np.ndarray:
+    h, w = PREPROCESS_SIZES[i]
+    return np.random.default_rng(100 + i).integers(0, 256, (h, w, 3), dtype=np.uint8)
+
+
+def preprocess_picks() -> np.ndarray:
+    n = 3 * 1008 * 1008
+    corners = [c * 1008 * 1008 + o for c in range(3) for o in (0, 1007, 1007 * 1008, n // 3 - 1)]
+    return np.unique(np.concatenate([np.random.default_rng(7).integers(0, n, 64), corners])).astype(np.int64)
+
+
+def preprocess_golden(ref: Reference) -> dict:
+    import hashlib
+    picks = preprocess_picks()
+    cases = []
+    for i, (h, w) in enumerate(PREPROCESS_SIZES):
+        out = ref.bilinear_resize_rgb(preprocess_image(i)).reshape(-1)
+        cases.append({"height": h, "width": w, "seed": 100 + i,
+                      "sha256": hashlib.sha256(out.astype("<f4").tobytes()).hexdigest(),
+                      "picks": [float(v) for v in out[picks]]})
+    return {"reference": "tools/sam3_vision_trunk.cpp:33-66 bilinear_resize_rgb via oracle/_ref",
+            "picks": [int(p) for p in picks], "cases": cases}
 
 
 def op_vectors(ref: Reference) -> dict[str, np.ndarray]:
@@ -121,10 +155,15 @@ def isa_spread(fmt: str, threads: int, gold: dict) -> dict:
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ops-only", action="store_true")
+    ap.add_argument("--preprocess-only", action="store_true")
     ap.add_argument("--formats", default="f16,q8_0,f32")
     ap.add_argument("--threads", type=int, default=8)
     a = ap.parse_args()
     ref = Reference()
+    (HERE / "preprocess.json").write_text(json.dumps(preprocess_golden(ref), indent=1))
+    print("preprocess.json written")
+    if a.preprocess_only:
+        return
     np.savez_compressed(HERE / "ops.npz", **op_vectors(ref))
     print("ops.npz written")
     if a.ops_only:
