@@ -265,7 +265,8 @@ class Reference:
         L.ref_to_float.argtypes = [C.c_int, _p, _i64, _p]
         L.ref_fp32_to_fp16.argtypes = [_p, _i64, _p]
         L.ref_patch_embed.argtypes = [C.c_int, _p, _p, _p, C.c_int]
-        L.ref_bilinear_resize_rgb.argtypes = [_p, C.c_int, C.c_int, _p]
+        if hasattr(L, "ref_bilinear_resize_rgb"):   # absent from the drop-in build
+            L.ref_bilinear_resize_rgb.argtypes = [_p, C.c_int, C.c_int, _p]
 
     def _check(self, rc):
         if rc != 0:
