@@ -410,6 +410,16 @@ def rgb8_extras(torch, dev, stream, trunk, s3t, batch=8, height=1080, width=1920
             "trunk_from_rgb8_images_per_s": round(batch / (ms_run / 1e3), 2)}
 
 
+def _cpu_model():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
 def cpu_baseline(fmt):
     """The reference's own CPU trunk (oracle/_ref: ggml CPU backend compiled
     from the reference sources) on one image with all host threads."""
@@ -418,10 +428,15 @@ def cpu_baseline(fmt):
         from sam3cpp_b200 import synthetic as syn
         ref = Reference()
         threads = os.cpu_count() or 1
-        _, sec = ref.trunk(syn.synthetic_gguf(fmt), syn.synthetic_image(0), threads)
+        path, img = syn.synthetic_gguf(fmt), syn.synthetic_image(0)
+        _, sec = ref.trunk(path, img, threads)
+        # also at the reference's as-shipped thread count (GGML_DEFAULT_N_THREADS = 4)
+        _, sec4 = ref.trunk(path, img, 4)
         return {"value": round(1.0 / sec, 5), "unit": "images/s", "cores": threads, "kind": "reference",
                 "sample": f"1 image, sam3::VisionTrunk::run ({fmt.upper()} GGUF), {sec:.1f} s, "
-                          f"{ref.path.name}"}
+                          f"{ref.path.name}",
+                "cpu_model": _cpu_model(),
+                "as_shipped_4_threads": {"value": round(1.0 / sec4, 5), "seconds": round(sec4, 2)}}
     except Exception as e:
         return {"value": None, "unit": "images/s", "cores": os.cpu_count(), "kind": "reference",
                 "sample": f"unavailable: {e}"}
