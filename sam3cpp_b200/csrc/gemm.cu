@@ -585,15 +585,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg::THREADS, 1)
             const uint32_t aph = (local >> 1) & 1;
             const int m = (tile / n_tiles_n) * 2 * kBM + int(rank) * kBM + row;
             const int n0 = (tile % n_tiles_n) * BN + col_grp * Cfg::WARP_COLS;
+            // kEpiResid: this row's fp32 residual for the first two 32-column
+            // chunks is loaded while the tile's mainloop is still running, the
+            // rest two chunks ahead of use (the residual is not written by
+            // anyone else before this epilogue).
+            float4 xres[2][8];
+            const bool row_ok = m < args.M;
             if constexpr (EPI == kEpiResid) {
-                // Pull this thread's residual slice (128 fp32 = 4 lines) into L2
-                // while the tile's mainloop is still running.
-                if (m < args.M) {
-                    const float* xr = args.resid + int64_t(m) * args.N + n0;
+                const float4* xr = reinterpret_cast<const float4*>(args.resid + int64_t(m) * args.N + n0);
 #pragma unroll
-                    for (int q = 0; q < Cfg::WARP_COLS / 32; ++q)
-                        if (n0 + 32 * q < args.N) prefetch_l2(xr + 32 * q);
-                }
+                for (int cc = 0; cc < 2; ++cc)
+#pragma unroll
+                    for (int q = 0; q < 8; ++q)
+                        xres[cc][q] = row_ok ? xr[cc * 8 + q] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                for (int q = 2; q < Cfg::WARP_COLS / 32; ++q)
+                    if (row_ok) prefetch_l2(args.resid + int64_t(m) * args.N + n0 + 32 * q);
             }
             if (!mbar_wait(tfull + acc, aph, args.status, kErrTimeoutEpilogue, abort_flag)) break;
             tc_fence_after();
@@ -668,6 +675,48 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg::THREADS, 1)
                             }
                         }
                         bulk_commit_group();
+                    }
+                }
+            } else if constexpr (EPI == kEpiResid) {
+                static_assert(Cfg::WARP_COLS % 64 == 0, "chunks come in pairs");
+                float4* xw = reinterpret_cast<float4*>(args.resid + int64_t(m) * args.N + n0);
+#pragma unroll
+                for (int c = 0; c < Cfg::WARP_COLS / 32; ++c) {
+                    const int n = n0 + c * 32;
+                    uint32_t r[32];
+                    tmem_ld32(tbase + c * 32, r);
+                    tmem_wait_ld();
+                    float4(&xc)[8] = xres[c & 1];
+                    if (row_ok) {
+                        // x = x + (acc + bias), two columns per packed operation
+                        const float4* bp = reinterpret_cast<const float4*>(args.bias + n);
+                        float v[32];
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) {
+                            const float4 bb = args.bias ? __ldg(bp + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+                            const float2 s0 = __fadd2_rn(
+                                make_float2(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1])),
+                                make_float2(bb.x, bb.y));
+                            const float2 s1 = __fadd2_rn(
+                                make_float2(__uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3])),
+                                make_float2(bb.z, bb.w));
+                            const float2 t0 = __fadd2_rn(make_float2(xc[q].x, xc[q].y), s0);
+                            const float2 t1 = __fadd2_rn(make_float2(xc[q].z, xc[q].w), s1);
+                            xw[c * 8 + q] = make_float4(t0.x, t0.y, t1.x, t1.y);
+                            v[4 * q] = t0.x; v[4 * q + 1] = t0.y; v[4 * q + 2] = t1.x; v[4 * q + 3] = t1.y;
+                        }
+                        if (args.out_nchw) {
+                            const int img = m / kTokens, t = m - img * kTokens;
+                            float* o = args.out_nchw + (int64_t(img) * args.N + n) * kTokens + t;
+#pragma unroll
+                            for (int i = 0; i < 32; ++i) o[int64_t(i) * kTokens] = v[i];
+                        }
+                        // the chunk two ahead reuses this register buffer
+                        if (c + 2 < Cfg::WARP_COLS / 32) {
+                            const float4* xr = reinterpret_cast<const float4*>(args.resid + int64_t(m) * args.N + n0);
+#pragma unroll
+                            for (int q = 0; q < 8; ++q) xc[q] = xr[(c + 2) * 8 + q];
+                        }
                     }
                 }
             } else {
