@@ -14,6 +14,11 @@ HBM; `e2e` = the same through the public API with pinned host buffers
 Inputs (780 MB of images, 0.9 GB of weights, ~8 GB of activations per step)
 are far larger than the 126 MB L2, so no explicit flush is done.
 
+After the timed regions, one eager pass of the same trunk records a CUDA
+event after every launch (s3t_trunk_profile): the roofline of the GEMM family,
+the attention and LayerNorm figures and `trunk_profile_ms` come from the
+trunk's own kernels at the bench's shape.
+
 Rank 0 prints one JSON line.
 """
 
@@ -205,8 +210,9 @@ def _run_ours(a, torch, dist, world, rank, local, dev):
     e2e_wall = time.perf_counter() - t0
     e2e_value = a.images * a.steps / (e2e_ms / 1e3)
 
-    # per-kernel live timing of the dominant kernels at this shape (outside the timed region)
-    kern = kernel_timings(torch, dev, stream, per)
+    # per-kernel device time of the trunk's own launches at this shape: one
+    # eager pass with a CUDA event after every launch, right after the timed region
+    prof = trunk.profile(imgs.data_ptr(), per, out.data_ptr(), stream.cuda_stream)
     extras = {}
     if rank == 0 and world == 1 and not a.no_extras:
         extras = config_extras(torch, dev, stream, trunk, syn, s3t)
@@ -219,9 +225,22 @@ def _run_ours(a, torch, dist, world, rank, local, dev):
         return
 
     bf16_peak, bf16_sus, hbm_peak, peak_kind = measured_peaks()
-    gemm_ms = kern["gemm_ms_per_layer"]
+    layers = prof["qkv"][1]
+    per_gemm = {k: prof[k][0] / max(prof[k][1], 1) for k in ("qkv", "proj", "fc1", "fc2")}
+    gemm_ms = sum(per_gemm.values())                     # one block's four GEMM launches
     gemm_flop = GEMM_FLOP_PER_IMAGE_LAYER * per
     achieved = gemm_flop / (gemm_ms / 1e3) / 1e12
+    attn = {}
+    for kind, key, n_groups, L in (("windowed", "attn_windowed", 9 * per, 576), ("global", "attn_global", per, 5184)):
+        ms, n = prof[key]
+        if n:
+            flop = 4.0 * n_groups * 16 * L * L * 64
+            attn[kind] = {"ms": round(ms / n, 4), "tflops": round(flop / (ms / n / 1e3) / 1e12, 1), "launches": n}
+    ln_ms, ln_n = prof["layernorm"]
+    ln_bytes = per * 5184 * 1024 * 6                     # read fp32 residual, write fp16 operand
+    norm = {"ms": round(ln_ms / max(ln_n, 1), 4), "launches": ln_n,
+            "gbs": round(ln_bytes / (ln_ms / max(ln_n, 1) / 1e3) / 1e9, 1)}
+    norm["frac_of_hbm"] = round(norm["gbs"] / hbm_peak, 4)
     line = {
         "metric": METRIC,
         "value": round(value, 3),
@@ -244,12 +263,15 @@ def _run_ours(a, torch, dist, world, rank, local, dev):
         },
         "roofline": {
             "bound": "tensor",
-            "kernel": "gemm_pair_kernel (qkv+proj+fc1+fc2 of one block, M=%d)" % (per * 5184),
+            "kernel": "gemm_pair_kernel: the trunk's QKV+RoPE, proj+residual, fc1+GELU, fc2+residual "
+                      "launches of one block (M=%d), per-launch CUDA events, averaged over %d blocks"
+                      % (per * 5184, layers),
             "achieved": round(achieved, 1), "peak": bf16_peak, "unit": "TFLOP/s",
             "frac": round(achieved / bf16_peak, 4), "peak_kind": f"{peak_kind} bf16 burst",
+            "frac_of_sustained": round(achieved / bf16_sus, 4) if bf16_sus else None,
             "traffic": GEMM_DRAM_BYTES_PER_IMAGE_LAYER * per,
             "traffic_note": "bytes per block's four GEMM launches; ncu 4-image capture scaled by images",
-            "per_gemm_ms": kern["per_gemm_ms"],
+            "per_gemm_ms": {k: round(v, 4) for k, v in per_gemm.items()},
             "trunk_tensor_frac": round(FLOP_PER_IMAGE * value / world / 1e12 / bf16_peak, 4),
         },
         "e2e": {"value": round(e2e_value, 3), "unit": "images/s",
@@ -258,7 +280,9 @@ def _run_ours(a, torch, dist, world, rank, local, dev):
                 "wall_s": round(e2e_wall, 3)},
         "clocks": clk.summary(),
         "gpu_launches": LAUNCHES_PER_TRUNK * a.steps * world,
-        "attention": kern["attention"],
+        "attention": attn,
+        "layernorm": norm,
+        "trunk_profile_ms": {k: round(v[0], 3) for k, v in prof.items()},
         **extras,
     }
     if world == 1 and not a.no_cpu_baseline:
@@ -266,45 +290,6 @@ def _run_ours(a, torch, dist, world, rank, local, dev):
     print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
-
-
-def kernel_timings(torch, dev, stream, per):
-    """CUDA-event time of each GEMM of one block and of both attention kinds
-    at the bench's shape, launched through the C ABI on `stream`."""
-    import ctypes as C
-    from sam3cpp_b200 import lib, check
-    L = lib()
-    M = per * 5184
-    g = torch.Generator(device=dev).manual_seed(0)
-    x = torch.randn((M, 4736), generator=g, device=dev, dtype=torch.float16)
-    shapes = {"qkv": (3072, 1024), "proj": (1024, 1024), "fc1": (4736, 1024), "fc2": (1024, 4736)}
-    res = {}
-    y = torch.empty((M, 4736), device=dev, dtype=torch.float16)
-    for name, (N, K) in shapes.items():
-        w = torch.randn((N, K), generator=g, device=dev, dtype=torch.float16) * 0.02
-        b = torch.zeros(N, device=dev)
-        xs = x[:, :K].contiguous()
-        def launch():
-            check(L.s3t_gemm_f16(dev.index, C.c_void_p(xs.data_ptr()), C.c_void_p(w.data_ptr()),
-                                 C.c_void_p(b.data_ptr()), M, N, K, 1 if name == "fc1" else 0, 0,
-                                 C.c_void_p(y.data_ptr()), C.c_void_p(stream.cuda_stream)))
-        res[name] = _event_ms(torch, dev, stream, launch, 5, 10)
-        del xs
-    att = {}
-    for kind, (groups, Lk) in {"windowed": (9 * per, 576), "global": (per, 5184)}.items():
-        q, k, v = (torch.randn((groups * 16, Lk, 64), generator=g, device=dev, dtype=torch.float16) for _ in range(3))
-        o = torch.empty((per * 5184, 1024), device=dev, dtype=torch.float16)
-        def launch():
-            check(L.s3t_attention(dev.index, C.c_void_p(q.data_ptr()), C.c_void_p(k.data_ptr()),
-                                  C.c_void_p(v.data_ptr()), groups, Lk, 1 if kind == "windowed" else 0, 0,
-                                  C.c_void_p(o.data_ptr()), C.c_void_p(stream.cuda_stream)))
-        ms = _event_ms(torch, dev, stream, launch, 3, 10)
-        flop = 4.0 * groups * 16 * Lk * Lk * 64
-        att[kind] = {"ms": round(ms, 4), "tflops": round(flop / (ms / 1e3) / 1e12, 1)}
-        del q, k, v, o
-    check(L.s3t_device_status(dev.index))
-    return {"gemm_ms_per_layer": sum(res.values()), "per_gemm_ms": {k: round(v, 4) for k, v in res.items()},
-            "attention": att, "traffic": None}
 
 
 def _event_ms(torch, dev, stream, fn, warm, reps):

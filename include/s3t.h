@@ -87,6 +87,16 @@ int s3t_trunk_run_layers(s3t_ctx *ctx, const float *images_nchw, int batch, int 
 int s3t_trunk_run_rgb8(s3t_ctx *ctx, const uint8_t *rgb, int width, int height, int batch, float *out_nchw,
                        int flags, void *stream);
 
+/* No counterpart in the reference: one eager (not graph-replayed) trunk run on
+ * device buffers with a CUDA event after every launch, for measurement.
+ * Returns per kernel class the summed device milliseconds and the launch
+ * count, in this order: 0 stem (im2col + patch GEMM + ln_pre/norm1),
+ * 1 QKV GEMM, 2 windowed attention, 3 global attention, 4 proj GEMM,
+ * 5 LayerNorm, 6 fc1 GEMM, 7 fc2 GEMM.  kind_ms and kind_launches hold 8
+ * entries each.  Synchronous. */
+int s3t_trunk_profile(s3t_ctx *ctx, const float *images_dev, int batch, float *out_dev, void *stream,
+                      double *kind_ms, int *kind_launches);
+
 /* Wait for the context's queued work and report any device-side error. */
 int s3t_sync(s3t_ctx *ctx, void *stream);
 

@@ -67,6 +67,7 @@ def lib() -> C.CDLL:
         L.s3t_stem_noalloc.argtypes = [p, p, i, p, p]
         L.s3t_trunk_run_rgb8.argtypes = [p, p, i, i, i, p, i, p]
         L.s3t_preprocess_rgb8.argtypes = [i, p, i, i, i, p, p]
+        L.s3t_trunk_profile.argtypes = [p, p, i, p, p, C.POINTER(C.c_double), C.POINTER(C.c_int)]
         _lib = L
     return _lib
 
@@ -211,6 +212,17 @@ class VisionTrunk:
         flags = (IMAGES_ON_DEVICE if images_on_device else 0) | (OUTPUT_ON_DEVICE if output_on_device else 0)
         check(lib().s3t_trunk_run(self.model.ctx, C.c_void_p(images_ptr), batch, C.c_void_p(out_ptr), flags,
                                   C.c_void_p(stream) if stream else None))
+
+    PROFILE_KINDS = ("stem", "qkv", "attn_windowed", "attn_global", "proj", "layernorm", "fc1", "fc2")
+
+    def profile(self, images_ptr: int, batch: int, out_ptr: int, stream: int = 0) -> dict:
+        """One eager trunk run on device buffers with a CUDA event after every
+        launch: {kernel class: (summed device ms, launches)}."""
+        ms = (C.c_double * 8)()
+        n = (C.c_int * 8)()
+        check(lib().s3t_trunk_profile(self.model.ctx, C.c_void_p(images_ptr), batch, C.c_void_p(out_ptr),
+                                      C.c_void_p(stream) if stream else None, ms, n))
+        return {k: (ms[i], n[i]) for i, k in enumerate(self.PROFILE_KINDS)}
 
     def sync(self, stream: int = 0) -> None:
         check(lib().s3t_sync(self.model.ctx, C.c_void_p(stream) if stream else None))

@@ -283,6 +283,8 @@ struct s3t_ctx {
     std::map<GraphKey, cudaGraphExec_t> graphs;
     cudaStream_t copy_in = nullptr, copy_out = nullptr;   // host-buffer pipelining
     std::vector<cudaEvent_t> events;
+    // Set only during s3t_trunk_profile: an event is recorded after every launch.
+    std::vector<std::pair<int, cudaEvent_t>>* prof = nullptr;
 };
 
 namespace {
@@ -327,11 +329,29 @@ int ensure_workspace(s3t_ctx* c, int batch) {
 }
 
 // Enqueue the whole trunk on `st` (called under stream capture).
+// Kernel classes of the per-launch profile (s3t_trunk_profile).
+enum { kProfStem = 0, kProfQkv, kProfAttnWin, kProfAttnGlob, kProfProj, kProfNorm, kProfFc1, kProfFc2, kProfKinds };
+
+int mark(s3t_ctx* c, cudaStream_t st, int kind) {
+    if (!c->prof) return 0;
+    cudaEvent_t e;
+    S3T_CUDA(cudaEventCreate(&e));
+    c->prof->emplace_back(kind, e);
+    S3T_CUDA(cudaEventRecord(e, st));
+    return 0;
+}
+
+#define S3T_MARK(kind) \
+    do {                                        \
+        if (mark(c, st, (kind))) return -1;     \
+    } while (0)
+
 int enqueue_trunk(s3t_ctx* c, const float* images, int batch, int n_layers, float* out, cudaStream_t st) {
     const int M = batch * kTokens;
     const int sms = c->dev->num_sms;
     int* status = c->dev->status;
     S3T_CUDA(cudaMemsetAsync(status, 0, sizeof(int), st));
+    S3T_MARK(-1);
     S3T_CUDA(launch_im2col(images, batch, c->cols, st));
 
     GemmArgs g{};
@@ -344,6 +364,7 @@ int enqueue_trunk(s3t_ctx* c, const float* images, int batch, int n_layers, floa
     S3T_CUDA(launch_gemm(c->cols, c->patch_w, g, kEpiPatch, sms, st));
     S3T_CUDA(launch_layernorm_stem(c->x, M, c->lnpre_w, c->lnpre_b, c->layers[0].n1w, c->layers[0].n1b, c->a16,
                                    c->layers[0].qkv_t == S3T_TYPE_Q8_0, st));
+    S3T_MARK(kProfStem);
 
     const int64_t qkv_stride = int64_t(M) * kDim;
     for (int l = 0; l < n_layers; ++l) {
@@ -360,6 +381,7 @@ int enqueue_trunk(s3t_ctx* c, const float* images, int batch, int n_layers, floa
         q.rope_global = c->dev->rope_global;
         q.status = status;
         S3T_CUDA(launch_gemm(c->a16, w.qkv, q, kEpiQkv, sms, st));
+        S3T_MARK(kProfQkv);
 
         AttnArgs at{};
         at.q = c->qkv;
@@ -374,6 +396,7 @@ int enqueue_trunk(s3t_ctx* c, const float* images, int batch, int n_layers, floa
         at.out = c->attn;
         at.status = status;
         S3T_CUDA(launch_attention(at, st));
+        S3T_MARK(glob ? kProfAttnGlob : kProfAttnWin);
 
         GemmArgs p{};
         p.M = M; p.N = kDim; p.K = kDim;
@@ -381,8 +404,10 @@ int enqueue_trunk(s3t_ctx* c, const float* images, int batch, int n_layers, floa
         p.resid = c->x;
         p.status = status;
         S3T_CUDA(launch_gemm(c->attn, w.proj, p, kEpiResid, sms, st));
+        S3T_MARK(kProfProj);
 
         S3T_CUDA(launch_layernorm(c->x, M, w.n2w, w.n2b, c->a16, w.fc1_t == S3T_TYPE_Q8_0, st));
+        S3T_MARK(kProfNorm);
 
         GemmArgs f1{};
         f1.M = M; f1.N = kMlp; f1.K = kDim;
@@ -392,6 +417,7 @@ int enqueue_trunk(s3t_ctx* c, const float* images, int batch, int n_layers, floa
         f1.q8 = w.fc2_t == S3T_TYPE_Q8_0;
         f1.status = status;
         S3T_CUDA(launch_gemm(c->a16, w.fc1, f1, kEpiF16, sms, st));
+        S3T_MARK(kProfFc1);
 
         GemmArgs f2{};
         f2.M = M; f2.N = kDim; f2.K = kMlp;
@@ -400,10 +426,12 @@ int enqueue_trunk(s3t_ctx* c, const float* images, int batch, int n_layers, floa
         f2.out_nchw = (l == n_layers - 1) ? out : nullptr;
         f2.status = status;
         S3T_CUDA(launch_gemm(c->h, w.fc2, f2, kEpiResid, sms, st));
+        S3T_MARK(kProfFc2);
 
         if (l + 1 < n_layers) {
             const LayerW& nx = c->layers[l + 1];
             S3T_CUDA(launch_layernorm(c->x, M, nx.n1w, nx.n1b, c->a16, nx.qkv_t == S3T_TYPE_Q8_0, st));
+            S3T_MARK(kProfNorm);
         }
     }
     return 0;
@@ -860,6 +888,37 @@ int s3t_trunk_run_rgb8(s3t_ctx* c, const uint8_t* rgb, int width, int height, in
     }
     S3T_CUDA(launch_resize_rgb8(src, width, height, batch, c->img, st));
     return run_impl(c, c->img, batch, c->n_layers, out, flags | S3T_IMAGES_ON_DEVICE, stream);
+}
+
+int s3t_trunk_profile(s3t_ctx* c, const float* images_dev, int batch, float* out_dev, void* stream, double* kind_ms,
+                      int* kind_launches) {
+    if (!c) return fail("ctx is null");
+    if (!c->finalized) return fail("weights not finalized (call s3t_finalize_weights)");
+    if (!images_dev || !out_dev || !kind_ms || !kind_launches) return fail("null argument to s3t_trunk_profile");
+    if (batch <= 0) return fail("batch must be positive");
+    S3T_CUDA(cudaSetDevice(c->device));
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+    if (ensure_workspace(c, batch)) return -1;
+    std::vector<std::pair<int, cudaEvent_t>> ev;
+    c->prof = &ev;
+    const int rc = enqueue_trunk(c, images_dev, batch, c->n_layers, out_dev, st);
+    c->prof = nullptr;
+    const cudaError_t se = cudaStreamSynchronize(st);
+    for (int k = 0; k < kProfKinds; ++k) {
+        kind_ms[k] = 0.0;
+        kind_launches[k] = 0;
+    }
+    for (size_t i = 1; rc == 0 && se == cudaSuccess && i < ev.size(); ++i) {
+        float ms = 0.f;
+        if (cudaEventElapsedTime(&ms, ev[i - 1].second, ev[i].second) == cudaSuccess && ev[i].first >= 0) {
+            kind_ms[ev[i].first] += ms;
+            kind_launches[ev[i].first] += 1;
+        }
+    }
+    for (auto& e : ev) cudaEventDestroy(e.second);
+    if (rc) return rc;
+    S3T_CUDA(se);
+    return check_status(c, st);
 }
 
 int s3t_sync(s3t_ctx* c, void* stream) {
