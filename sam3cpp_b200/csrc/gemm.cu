@@ -416,8 +416,9 @@ __global__ void __launch_bounds__(192, 1)
 // producer and UMMA threads, so every instruction they issue can delay the
 // mainloop: the UMMA loop uses descriptors built once, the fp32 epilogue
 // math runs as packed f32x2 operations (two columns per instruction), and the
-// plain fp16 output (kEpiF16) leaves through shared memory and one TMA store
-// per 32 x 32 chunk instead of 32 scattered row stores.
+// outputs (fp16 for kEpiF16 / kEpiQkv, the fp32 residual for kEpiResid) leave
+// through shared memory and one TMA store per 32 x 32 chunk instead of 32
+// scattered row stores.
 struct PairCfg {
     static constexpr int BN = 256;
     static constexpr int STAGES = 6;
@@ -430,7 +431,9 @@ struct PairCfg {
     // kEpiF16 stages each 32x32 output chunk in shared memory (2 KB buffers,
     // 64-byte swizzle) and stores it with TMA.
     static constexpr int OUT_BUFS = EPI_WARPS <= 8 ? 2 : 1;
-    __host__ __device__ static constexpr bool staged_out(int EPI) { return EPI == kEpiF16 || EPI == kEpiQkv; }
+    __host__ __device__ static constexpr bool staged_out(int EPI) {
+        return EPI == kEpiF16 || EPI == kEpiQkv || EPI == kEpiResid;
+    }
     static constexpr uint32_t OUT_BYTES = OUT_BUFS * 2048;
     template <int EPI>
     static constexpr size_t smem() {
@@ -679,7 +682,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg::THREADS, 1)
                 }
             } else if constexpr (EPI == kEpiResid) {
                 static_assert(Cfg::WARP_COLS % 64 == 0, "chunks come in pairs");
-                float4* xw = reinterpret_cast<float4*>(args.resid + int64_t(m) * args.N + n0);
+                // The updated rows leave through a 4 KB shared-memory stage
+                // (32 rows x 128 B, 128-byte swizzle) and one TMA store per chunk.
+                uint8_t* stage = sOut + (warp - 2) * Cfg::OUT_BYTES;
+                const int row0 = m - lane;
 #pragma unroll
                 for (int c = 0; c < Cfg::WARP_COLS / 32; ++c) {
                     const int n = n0 + c * 32;
@@ -687,24 +693,36 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg::THREADS, 1)
                     tmem_ld32(tbase + c * 32, r);
                     tmem_wait_ld();
                     float4(&xc)[8] = xres[c & 1];
-                    if (row_ok) {
-                        // x = x + (acc + bias), two columns per packed operation
-                        const float4* bp = reinterpret_cast<const float4*>(args.bias + n);
-                        float v[32];
+                    // x = x + (acc + bias), two columns per packed operation
+                    const float4* bp = reinterpret_cast<const float4*>(args.bias + n);
+                    float v[32];
 #pragma unroll
-                        for (int q = 0; q < 8; ++q) {
-                            const float4 bb = args.bias ? __ldg(bp + q) : make_float4(0.f, 0.f, 0.f, 0.f);
-                            const float2 s0 = __fadd2_rn(
-                                make_float2(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1])),
-                                make_float2(bb.x, bb.y));
-                            const float2 s1 = __fadd2_rn(
-                                make_float2(__uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3])),
-                                make_float2(bb.z, bb.w));
-                            const float2 t0 = __fadd2_rn(make_float2(xc[q].x, xc[q].y), s0);
-                            const float2 t1 = __fadd2_rn(make_float2(xc[q].z, xc[q].w), s1);
-                            xw[c * 8 + q] = make_float4(t0.x, t0.y, t1.x, t1.y);
-                            v[4 * q] = t0.x; v[4 * q + 1] = t0.y; v[4 * q + 2] = t1.x; v[4 * q + 3] = t1.y;
-                        }
+                    for (int q = 0; q < 8; ++q) {
+                        const float4 bb = args.bias ? __ldg(bp + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+                        const float2 s0 = __fadd2_rn(
+                            make_float2(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1])),
+                            make_float2(bb.x, bb.y));
+                        const float2 s1 = __fadd2_rn(
+                            make_float2(__uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3])),
+                            make_float2(bb.z, bb.w));
+                        const float2 t0 = __fadd2_rn(make_float2(xc[q].x, xc[q].y), s0);
+                        const float2 t1 = __fadd2_rn(make_float2(xc[q].z, xc[q].w), s1);
+                        v[4 * q] = t0.x; v[4 * q + 1] = t0.y; v[4 * q + 2] = t1.x; v[4 * q + 3] = t1.y;
+                    }
+                    if (lane == 0) bulk_wait_group_read<0>();   // the previous chunk's store has read the stage
+                    __syncwarp();
+                    uint8_t* rowp = stage + lane * 128;
+#pragma unroll
+                    for (int q = 0; q < 8; ++q)
+                        *reinterpret_cast<float4*>(rowp + ((q ^ (lane & 7)) << 4)) =
+                            make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        if (row0 < args.M) tma_store_2d(&tmC, stage, n, row0);
+                        bulk_commit_group();
+                    }
+                    if (row_ok) {
                         if (args.out_nchw) {
                             const int img = m / kTokens, t = m - img * kTokens;
                             float* o = args.out_nchw + (int64_t(img) * args.N + n) * kTokens + t;
@@ -794,6 +812,10 @@ cudaError_t launch_pair(const __half* A, const __half* B, const GemmArgs& args, 
     if (EPI == kEpiF16 &&
         !make_tmap_2d(&tc, args.out16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, args.N, args.M, 32, 32,
                       CU_TENSOR_MAP_SWIZZLE_64B))
+        return cudaErrorInvalidValue;
+    if (EPI == kEpiResid &&
+        !make_tmap_2d(&tc, args.resid, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, args.N, args.M, 32, 32,
+                      CU_TENSOR_MAP_SWIZZLE_128B))
         return cudaErrorInvalidValue;
     if (EPI == kEpiQkv) {
         // q, k, v: qkv_stride elements each, contiguous; one plane per (group, head).
