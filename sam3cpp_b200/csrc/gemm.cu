@@ -135,20 +135,35 @@ __device__ __forceinline__ void qkv_chunk(const GemmArgs& a, int m, int n, const
     }
     if ((n >> 10) < 2) {
         const QkvPos p = qkv_pos(m, a.windowed);
-        const float* tab = a.windowed ? a.rope_local : a.rope_global;
         const int half = (n >> 5) & 1;
-        const float4* cs = reinterpret_cast<const float4*>(tab + (half ? p.py : p.px) * 32);   // [pos][cos16 | sin16]
+        float c[16], s[16];
+        if (half) {
+            // y position: the same for (nearly) every row of a warp, so the
+            // row-major table is read as broadcasts
+            const float* tab = a.windowed ? a.rope_local : a.rope_global;
+            const float4* cs = reinterpret_cast<const float4*>(tab + p.py * 32);   // [pos][cos16 | sin16]
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const float4 c4 = __ldg(cs + q), s4 = __ldg(cs + 4 + q);
-            const float c[4] = {c4.x, c4.y, c4.z, c4.w}, s[4] = {s4.x, s4.y, s4.z, s4.w};
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const int j = 4 * q + u;
-                // (x0, x1) -> (x0 c - x1 s, x0 s + x1 c)
-                v[j] = __ffma2_rn(make_float2(v[j].x, v[j].x), make_float2(c[u], s[u]),
-                                  __fmul2_rn(make_float2(v[j].y, v[j].y), make_float2(-s[u], c[u])));
+            for (int q = 0; q < 4; ++q) {
+                const float4 c4 = __ldg(cs + q), s4 = __ldg(cs + 4 + q);
+                c[4 * q] = c4.x; c[4 * q + 1] = c4.y; c[4 * q + 2] = c4.z; c[4 * q + 3] = c4.w;
+                s[4 * q] = s4.x; s[4 * q + 1] = s4.y; s[4 * q + 2] = s4.z; s[4 * q + 3] = s4.w;
             }
+        } else {
+            // x position: consecutive rows of a warp have consecutive positions,
+            // so the transposed table gives one contiguous 4-byte load per lane
+            const float* tt = a.windowed ? a.rope_local_t : a.rope_global_t;
+            const int P = a.windowed ? kWindow : kGrid;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                c[j] = __ldg(tt + j * P + p.px);
+                s[j] = __ldg(tt + (16 + j) * P + p.px);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            // (x0, x1) -> (x0 c - x1 s, x0 s + x1 c)
+            v[j] = __ffma2_rn(make_float2(v[j].x, v[j].x), make_float2(c[j], s[j]),
+                              __fmul2_rn(make_float2(v[j].y, v[j].y), make_float2(-s[j], c[j])));
         }
     }
 #pragma unroll

@@ -45,6 +45,8 @@ struct GemmArgs {
     int windowed;             // kEpiQkv: 24x24 windows (1) or whole image (0)
     const float* rope_local;  // [24][2][16] cos,sin for scale 1
     const float* rope_global; // [72][2][16] cos,sin for scale 24/72
+    const float* rope_local_t;  // the same tables transposed: [2][16][24]
+    const float* rope_global_t; // [2][16][72]
     int* status;              // device status word
 };
 

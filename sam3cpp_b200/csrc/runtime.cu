@@ -85,6 +85,8 @@ struct DeviceState {
     int num_sms = 0;
     float* rope_local = nullptr;
     float* rope_global = nullptr;
+    float* rope_local_t = nullptr;    // [cos|sin][16][pos]: one frequency of consecutive positions is contiguous
+    float* rope_global_t = nullptr;
     int* status = nullptr;
 };
 
@@ -111,6 +113,16 @@ int device_state(int device, DeviceState** out) {
         S3T_CUDA(cudaMemcpy(d.rope_local, rl.data(), rl.size() * 4, cudaMemcpyHostToDevice));
         S3T_CUDA(cudaMemcpy(d.rope_global, rg.data(), rg.size() * 4, cudaMemcpyHostToDevice));
         S3T_CUDA(cudaMemset(d.status, 0, sizeof(int)));
+        for (int g = 0; g < 2; ++g) {
+            const std::vector<float>& tab = g ? rg : rl;
+            const int P = g ? kGrid : kWindow;
+            std::vector<float> t(tab.size());
+            for (int pos = 0; pos < P; ++pos)
+                for (int r = 0; r < 32; ++r) t[size_t(r) * P + pos] = tab[size_t(pos) * 32 + r];
+            float** dst = g ? &d.rope_global_t : &d.rope_local_t;
+            S3T_CUDA(cudaMalloc(dst, t.size() * 4));
+            S3T_CUDA(cudaMemcpy(*dst, t.data(), t.size() * 4, cudaMemcpyHostToDevice));
+        }
         d.ready = true;
     }
     *out = &d;
@@ -379,6 +391,8 @@ int enqueue_trunk(s3t_ctx* c, const float* images, int batch, int n_layers, floa
         q.windowed = glob ? 0 : 1;
         q.rope_local = c->dev->rope_local;
         q.rope_global = c->dev->rope_global;
+        q.rope_local_t = c->dev->rope_local_t;
+        q.rope_global_t = c->dev->rope_global_t;
         q.status = status;
         S3T_CUDA(launch_gemm(c->a16, w.qkv, q, kEpiQkv, sms, st));
         S3T_MARK(kProfQkv);
