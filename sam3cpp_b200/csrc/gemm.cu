@@ -434,11 +434,18 @@ __global__ void __launch_bounds__(192, 1)
 // outputs (fp16 for kEpiF16 / kEpiQkv, the fp32 residual for kEpiResid) leave
 // through shared memory and one TMA store per 32 x 32 chunk instead of 32
 // scattered row stores.
-struct PairCfg {
+template <int BK_>
+struct PairCfgT {
     static constexpr int BN = 256;
-    static constexpr int STAGES = 6;
-    static constexpr uint32_t A_BYTES = kBM * kBK * 2;          // this CTA's 128 rows of A
-    static constexpr uint32_t B_BYTES = (BN / 2) * kBK * 2;     // this CTA's 128 rows of B
+    // A stage holds BK K-columns as 64-column (128-byte) swizzle atoms.  With
+    // BK = 128 the lone UMMA thread waits, issues and commits once per 8
+    // UMMAs (K = 1024 GEMMs); the long-K fc2 keeps 64-column stages, 6 deep.
+    static constexpr int BK = BK_;
+    static constexpr int STAGES = BK_ == 128 ? 3 : 6;
+    static constexpr uint32_t ATOM_A = kBM * 64 * 2;            // 128 rows x 64 K-columns
+    static constexpr uint32_t ATOM_B = (BN / 2) * 64 * 2;
+    static constexpr uint32_t A_BYTES = ATOM_A * (BK / 64);     // this CTA's 128 rows of A
+    static constexpr uint32_t B_BYTES = ATOM_B * (BK / 64);     // this CTA's 128 rows of B
     static constexpr uint32_t TMEM_COLS = 2 * BN;
     static constexpr int EPI_WARPS = 8;
     static constexpr int COL_GROUPS = EPI_WARPS / 4;            // warps per TMEM lane quarter
@@ -456,12 +463,13 @@ struct PairCfg {
     }
     static constexpr int THREADS = 64 + 32 * EPI_WARPS;
 };
+using PairCfg = PairCfgT<128>;
 
-template <int EPI>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg::THREADS, 1)
+template <int EPI, int BK>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfgT<BK>::THREADS, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmC, const GemmArgs args) {
-    using Cfg = PairCfg;
+    using Cfg = PairCfgT<BK>;
     constexpr int STAGES = Cfg::STAGES, BN = Cfg::BN;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -482,7 +490,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg::THREADS, 1)
     const int n_tiles_n = (args.N + BN - 1) / BN;
     const int n_tiles = ((args.M + 2 * kBM - 1) / (2 * kBM)) * n_tiles_n;
     const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
-    const int num_kb = args.K / kBK;
+    const int num_kb = args.K / Cfg::BK;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -491,7 +499,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg::THREADS, 1)
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(tfull + i, 1);
-            mbar_init(tempty + i, 2 * PairCfg::EPI_WARPS);   // every epilogue warp of the pair
+            mbar_init(tempty + i, 2 * Cfg::EPI_WARPS);   // every epilogue warp of the pair
         }
         mbar_init(drain, 1);
         *abort_flag = 0;
@@ -530,8 +538,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg::THREADS, 1)
                         armed |= 1u << s;
                         armed_parity = (armed_parity & ~(1u << s)) | (ph << s);
                     }
-                    tma_load_2d_pair(sA + s * Cfg::A_BYTES, &tmA, lfull, kb * kBK, m0);
-                    tma_load_2d_pair(sB + s * Cfg::B_BYTES, &tmB, lfull, kb * kBK, n0);
+#pragma unroll
+                    for (int at = 0; at < Cfg::BK / 64; ++at) {
+                        tma_load_2d_pair(sA + s * Cfg::A_BYTES + at * Cfg::ATOM_A, &tmA, lfull, kb * Cfg::BK + at * 64, m0);
+                        tma_load_2d_pair(sB + s * Cfg::B_BYTES + at * Cfg::ATOM_B, &tmB, lfull, kb * Cfg::BK + at * 64, n0);
+                    }
                     if (++s == STAGES) {
                         s = 0;
                         ph ^= 1;
@@ -574,8 +585,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg::THREADS, 1)
                     const uint64_t da = dA0 + uint64_t(s) * (Cfg::A_BYTES >> 4);
                     const uint64_t db = dB0 + uint64_t(s) * (Cfg::B_BYTES >> 4);
 #pragma unroll
-                    for (int k = 0; k < kBK / 16; ++k)
-                        umma_f16_ss_pair(d_tmem, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0);
+                    for (int k = 0; k < Cfg::BK / 16; ++k)
+                        umma_f16_ss_pair(d_tmem, da + (k / 4) * (Cfg::ATOM_A >> 4) + 2 * (k % 4),
+                                         db + (k / 4) * (Cfg::ATOM_B >> 4) + 2 * (k % 4), idesc, (kb | k) != 0);
                     issued = true;
                     umma_commit_pair(empty + s, 0x3);
                     if (++s == STAGES) {
@@ -813,8 +825,9 @@ cudaError_t launch_bn(const __half* A, const __half* B, const GemmArgs& args, in
 // gemm_prepare; one process drives one device at a time in this library).
 int g_pair_capacity = 0;
 
-template <int EPI>
-cudaError_t launch_pair(const __half* A, const __half* B, const GemmArgs& args, int num_sms, cudaStream_t stream) {
+template <int EPI, int BK>
+cudaError_t launch_pair_bk(const __half* A, const __half* B, const GemmArgs& args, int num_sms, cudaStream_t stream) {
+    using Cfg = PairCfgT<BK>;
     CUtensorMap ta, tb;
     if (!make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, args.K, args.M, kBK, kBM)) return cudaErrorInvalidValue;
     if (!make_tmap_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, args.K, args.N, kBK, PairCfg::BN / 2))
@@ -840,14 +853,23 @@ cudaError_t launch_pair(const __half* A, const __half* B, const GemmArgs& args, 
                           3 * uint64_t(args.qkv_stride) / (L * kHeadDim), 32, 8, CU_TENSOR_MAP_SWIZZLE_64B))
             return cudaErrorInvalidValue;
     }
-    gemm_pair_kernel<EPI><<<2 * pairs, PairCfg::THREADS, PairCfg::smem<EPI>(), stream>>>(ta, tb, tc, args);
+    gemm_pair_kernel<EPI, BK><<<2 * pairs, Cfg::THREADS, Cfg::template smem<EPI>(), stream>>>(ta, tb, tc, args);
     return cudaGetLastError();
 }
 
 template <int EPI>
+cudaError_t launch_pair(const __half* A, const __half* B, const GemmArgs& args, int num_sms, cudaStream_t stream) {
+    return args.K >= 2048 ? launch_pair_bk<EPI, 64>(A, B, args, num_sms, stream)
+                          : launch_pair_bk<EPI, 128>(A, B, args, num_sms, stream);
+}
+
+template <int EPI>
 cudaError_t prepare_pair() {
-    return cudaFuncSetAttribute(gemm_pair_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                int(PairCfg::smem<EPI>()));
+    const cudaError_t e = cudaFuncSetAttribute(gemm_pair_kernel<EPI, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               int(PairCfgT<128>::smem<EPI>()));
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(gemm_pair_kernel<EPI, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(PairCfgT<64>::smem<EPI>()));
 }
 
 template <int BN, int EPI>
@@ -882,7 +904,8 @@ cudaError_t gemm_prepare() {
         attr.val.clusterDim.z = 1;
         cfg.attrs = &attr;
         cfg.numAttrs = 1;
-        if (cudaOccupancyMaxActiveClusters(&clusters, gemm_pair_kernel<kEpiF16>, &cfg) == cudaSuccess && clusters > 0)
+        if (cudaOccupancyMaxActiveClusters(&clusters, gemm_pair_kernel<kEpiF16, 128>, &cfg) == cudaSuccess &&
+            clusters > 0)
             g_pair_capacity = clusters;
         else
             g_pair_capacity = sms / 2;
@@ -925,7 +948,7 @@ cudaError_t launch_gemm(const __half* A, const __half* B, const GemmArgs& args, 
     // N = 1024 / 3072 / 4736: CTA-pair 256 x 256 tiles (4736 leaves one half
     // tile); narrow problems use single-CTA 128 x 128 tiles.
     const bool wide = args.N >= 1024;
-    if (wide && num_sms >= 2) {
+    if (wide && num_sms >= 2 && args.K % (args.K >= 2048 ? 64 : 128) == 0) {
         switch (epi) {
             case kEpiF16: return launch_pair<kEpiF16>(A, B, args, num_sms, stream);
             case kEpiQkv: return launch_pair<kEpiQkv>(A, B, args, num_sms, stream);
