@@ -149,3 +149,24 @@ def test_full_trunk_vs_reference_golden(gpu, fmt):
     assert r <= tol and c >= COS_TOL, (fmt, r, c, tol)
     assert abs(float(got.astype(np.float64).mean()) - float(gold["mean"])) < 2e-2 * float(gold["std"])
     assert abs(float(got.std()) - float(gold["std"])) < 1e-2 * float(gold["std"])
+
+
+def test_trunk_profile_pass(gpu, torch_cuda):
+    """s3t_trunk_profile: an eager pass with per-launch events gives the same
+    output as the graph-replayed trunk and counts every launch of the
+    8-layer (one global block) model."""
+    from sam3cpp_b200 import synthetic as s
+    torch = torch_cuda
+    path, _ = _models("f16", 8, True)
+    trunk = gpu.VisionTrunk(gpu.GgufModel(path))
+    imgs = torch.from_numpy(s.synthetic_images(2)).cuda()
+    out_a = torch.empty((2, 1024, 72, 72), device="cuda")
+    out_b = torch.empty_like(out_a)
+    trunk.run_device(imgs.data_ptr(), 2, out_a.data_ptr())
+    trunk.sync()
+    prof = trunk.profile(imgs.data_ptr(), 2, out_b.data_ptr())
+    assert torch.equal(out_a, out_b)
+    counts = {k: v[1] for k, v in prof.items()}
+    assert counts == {"stem": 1, "qkv": 8, "attn_windowed": 7, "attn_global": 1, "proj": 8,
+                      "layernorm": 15, "fc1": 8, "fc2": 8}
+    assert all(v[0] > 0 for v in prof.values())
