@@ -44,8 +44,9 @@ FLOP_PER_IMAGE = 5.3986e12          # GEMMs 4609.6 GF + attention 782.8 GF + pat
 GEMM_FLOP_PER_IMAGE_LAYER = 144.05e9  # 2*T*C*(3C + C + 2F), T=5184, C=1024, F=4736
 LAUNCHES_PER_TRUNK = 3 + 32 * 6 + 31  # im2col, patch GEMM, stem LN; 6 per block; 31 inter-block LNs
 # DRAM bytes (read + write) of the four GEMM launches of one block, per image:
-# ncu capture of the 4-image trunk (profiles/gemm_pair_4img.md: 130 + 160 +
-# 197 + 389 MB), scaled by the images a launch processes.
+# one ncu capture of the four GEMM launches of block 0 of a 4-image trunk
+# (QKV 130 + proj 160 + fc1 197 + fc2 389 MB), scaled by the images a launch
+# processes.
 GEMM_DRAM_BYTES_PER_IMAGE_LAYER = 876e6 / 4
 
 
