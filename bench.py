@@ -155,7 +155,9 @@ def _run_ours(a, torch, dist, world, rank, local, dev):
     if world > 1:
         dist.barrier()
     path = syn.synthetic_gguf(a.format)
+    t_load = time.perf_counter()
     model = s3t.GgufModel(path, device=local)
+    load_s = time.perf_counter() - t_load   # GGUF read + upload + fp16 conversion, once per context
     trunk = s3t.VisionTrunk(model)
 
     imgs_host = torch.from_numpy(syn.synthetic_images(per, start=rank * per)).pin_memory()
@@ -284,6 +286,7 @@ def _run_ours(a, torch, dist, world, rank, local, dev):
         "attention": attn,
         "layernorm": norm,
         "trunk_profile_ms": {k: round(v[0], 3) for k, v in prof.items()},
+        "model_load_s": round(load_s, 3),
         **extras,
     }
     if world == 1 and not a.no_cpu_baseline:
