@@ -133,6 +133,14 @@ int s3t_rope(int device, void *x, int groups, int L, int windowed, int bf16, voi
 int s3t_layernorm(int device, const float *x, int rows, const float *gamma, const float *beta, void *y16, int q8,
                   void *stream);
 
+/* No counterpart in the reference: failure-detection self-test.  One device
+ * thread waits, for limit_ms (1..2000), on an mbarrier that nothing arrives
+ * at; the bounded wait gives up, records a timeout in the device status word
+ * and the kernel returns.  Returns 0 when the wait gave up as designed; the
+ * next s3t_device_status(device) then reports (and clears) the timeout, and
+ * the device stays usable. */
+int s3t_selftest_wait_timeout(int device, int limit_ms);
+
 /* Synchronize `device` and report (then clear) the device status word that
  * the op-level entry points write when a bounded in-kernel wait times out. */
 int s3t_device_status(int device);

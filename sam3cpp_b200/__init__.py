@@ -68,6 +68,7 @@ def lib() -> C.CDLL:
         L.s3t_trunk_run_rgb8.argtypes = [p, p, i, i, i, p, i, p]
         L.s3t_preprocess_rgb8.argtypes = [i, p, i, i, i, p, p]
         L.s3t_trunk_profile.argtypes = [p, p, i, p, p, C.POINTER(C.c_double), C.POINTER(C.c_int)]
+        L.s3t_selftest_wait_timeout.argtypes = [i, i]
         _lib = L
     return _lib
 

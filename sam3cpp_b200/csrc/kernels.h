@@ -22,6 +22,7 @@ enum : int {
     kErrTimeoutMma = 2,
     kErrTimeoutEpilogue = 3,
     kErrTimeoutDrain = 4,
+    kErrTimeoutProbe = 5,    // the wait-timeout self-test (s3t_selftest_wait_timeout)
 };
 
 enum GemmEpilogue : int {
@@ -82,6 +83,10 @@ cudaError_t launch_layernorm_stem(float* x, int rows, const float* g0, const flo
 // ic*196 + kh*14 + kw, zero beyond 588.  round_f16: the pixel values become
 // fp16 (true for every weight format: the MMA operands are fp16).
 cudaError_t launch_im2col(const float* images, int batch, __half* cols, cudaStream_t stream);
+// One thread waits (limit_ns) on an mbarrier nothing arrives at; *gave_up = 1
+// and kErrTimeoutProbe in *status when the bounded wait ran out.
+cudaError_t launch_wait_timeout_probe(int* status, uint64_t limit_ns, int* gave_up, cudaStream_t stream);
+
 // uint8 RGB [batch][height][width][3] -> normalized [batch][3][1008][1008] fp32
 // (the reference's bilinear_resize_rgb, bit-exact).
 cudaError_t launch_resize_rgb8(const uint8_t* rgb, int width, int height, int batch, float* out, cudaStream_t stream);

@@ -64,20 +64,25 @@ S3T_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Bounded wait for the phase with the given parity.  Returns false (after
 // recording `code` in *status) if the phase did not complete in time, or if
 // another role of the CTA already gave up (*abort set).
-S3T_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code, volatile int* abort) {
+S3T_DEV bool mbar_wait_limit(uint64_t* bar, uint32_t parity, int* status, int code, volatile int* abort,
+                             uint64_t limit_ns) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
     for (uint32_t i = 1;; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((i & 255u) == 0) {
             if (abort && *abort) return false;
-            if (globaltimer() - t0 > kWaitLimitNs) {
+            if (globaltimer() - t0 > limit_ns) {
                 report_error(status, code);
                 if (abort) *abort = 1;
                 return false;
             }
         }
     }
+}
+
+S3T_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code, volatile int* abort) {
+    return mbar_wait_limit(bar, parity, status, code, abort, kWaitLimitNs);
 }
 
 // ------------------------------------------------------------------ TMA ---

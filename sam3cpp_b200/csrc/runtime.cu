@@ -135,6 +135,7 @@ const char* status_message(int code) {
         case kErrTimeoutMma: return "device wait timed out in an MMA issuer";
         case kErrTimeoutEpilogue: return "device wait timed out in an epilogue/softmax warp";
         case kErrTimeoutDrain: return "device wait timed out while draining after an error";
+        case kErrTimeoutProbe: return "device wait timed out in the wait-timeout self-test";
     }
     return "unknown device error";
 }
@@ -1023,6 +1024,24 @@ int s3t_preprocess_rgb8(int device, const uint8_t* rgb, int width, int height, i
     S3T_CUDA(cudaSetDevice(device));
     S3T_CUDA(launch_resize_rgb8(rgb, width, height, batch, out, static_cast<cudaStream_t>(stream)));
     return 0;
+}
+
+int s3t_selftest_wait_timeout(int device, int limit_ms) {
+    DeviceState* ds = nullptr;
+    if (device_state(device, &ds)) return -1;
+    if (limit_ms < 1 || limit_ms > 2000) return fail("limit_ms must be in [1, 2000]");
+    S3T_CUDA(cudaSetDevice(device));
+    int* gave_up = nullptr;
+    S3T_CUDA(cudaMalloc(&gave_up, sizeof(int)));
+    S3T_CUDA(cudaMemset(gave_up, 0, sizeof(int)));
+    cudaError_t e = launch_wait_timeout_probe(ds->status, uint64_t(limit_ms) * 1000000ull, gave_up, nullptr);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    int h = 0;
+    if (e == cudaSuccess) e = cudaMemcpy(&h, gave_up, sizeof(int), cudaMemcpyDeviceToHost);
+    cudaFree(gave_up);
+    S3T_CUDA(e);
+    if (!h) return fail("self-test: the bounded wait did not give up");
+    return 0;   // the timeout is now in the device status word (s3t_device_status reports it)
 }
 
 int s3t_device_status(int device) {

@@ -156,3 +156,22 @@ def test_rope(s3t, torch_cuda, oracle, windowed):
     ref = oracle.rope_axial(xin.transpose(1, 0, 2), pos % grid, pos // grid, 1.0 if windowed else 24 / 72)
     got = xd.float().cpu().numpy().transpose(1, 0, 2)
     assert rel_l2(got, ref) < 1e-3
+
+
+def test_bounded_wait_reports_timeout_and_device_stays_usable(s3t, torch_cuda):
+    """Failure detection without a GPU fault: a device wait on an mbarrier that
+    nothing arrives at gives up after its limit (100 ms here), the status word
+    reports the timeout once, and the next kernels run normally."""
+    torch = torch_cuda
+    _ok(s3t, s3t.s3t_device_status(0))
+    _ok(s3t, s3t.s3t_selftest_wait_timeout(0, 100))
+    assert s3t.s3t_device_status(0) != 0
+    assert "self-test" in s3t.s3t_last_error().decode()
+    _ok(s3t, s3t.s3t_device_status(0))          # reported once, then cleared
+    x = torch.randn(256, 1024, device="cuda", dtype=torch.float16)
+    w = torch.randn(1024, 1024, device="cuda", dtype=torch.float16) * 0.02
+    y = torch.empty(256, 1024, device="cuda", dtype=torch.float16)
+    _ok(s3t, s3t.s3t_gemm_f16(0, _p(x), _p(w), None, 256, 1024, 1024, 0, 0, _p(y), None))
+    _ok(s3t, s3t.s3t_device_status(0))
+    ref = x.float() @ w.float().t()
+    assert float((y.float() - ref).norm() / ref.norm()) < 1e-3
