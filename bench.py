@@ -344,6 +344,41 @@ def attention_microbench(torch, dev, stream, images=32):
     return res
 
 
+def encoder_attention_extras(torch, dev, stream, s3t, images=4):
+    """The encoder fusion's attention (s3t_mha_d32: 8 heads of 32): self
+    attention over the 72x72 image tokens of `images` images (one launch per
+    image, no mask) and image-to-prompt cross attention (5184 queries, 33
+    prompt keys of which 9 are masked).  fp16 q/k/v ~ N(0, 1.5^2), seed 6."""
+    peak = measured_peaks()[0]
+    g = torch.Generator(device=dev).manual_seed(6)
+    T = 5184
+    q, k, v = ((torch.randn((images, T, 256), generator=g, device=dev) * 1.5).half() for _ in range(3))
+    o = torch.empty((images, T, 256), device=dev)
+    kp, vp = ((torch.randn((33, 256), generator=g, device=dev) * 1.5).half() for _ in range(2))
+    mask = torch.zeros(33, device=dev)
+    mask[24:] = float("-inf")
+    op = torch.empty((T, 256), device=dev)
+    sp = stream.cuda_stream
+
+    def self_attn():
+        for i in range(images):
+            s3t.mha_d32(dev.index, q[i].data_ptr(), k[i].data_ptr(), v[i].data_ptr(), T, T, None, o[i].data_ptr(),
+                        0, sp)
+
+    def cross_attn():
+        s3t.mha_d32(dev.index, q[0].data_ptr(), kp.data_ptr(), vp.data_ptr(), T, 33, mask.data_ptr(),
+                    op.data_ptr(), 0, sp)
+
+    ms_self = _event_ms(torch, dev, stream, self_attn, 3, 10)
+    ms_cross = _event_ms(torch, dev, stream, cross_attn, 3, 20)
+    check_status = s3t.lib().s3t_device_status(dev.index)
+    flop = 4.0 * images * T * T * 32 * 8
+    tf = flop / (ms_self / 1e3) / 1e12
+    return {"self_shape": f"{images}x{T}x{T}x8x32", "self_ms": round(ms_self, 4), "self_tflops": round(tf, 1),
+            "self_frac_of_bf16_peak": round(tf / peak, 4), "cross_shape": f"{T}x33(9 masked)x8x32",
+            "cross_ms": round(ms_cross, 4), "status": check_status}
+
+
 def config_extras(torch, dev, stream, trunk, syn, s3t):
     """Single-GPU extras: b=1 F16 p50 latency (device in -> device out),
     Q8_0 batch-8 throughput and the bf16 attention microbenchmark."""
@@ -373,6 +408,10 @@ def config_extras(torch, dev, stream, trunk, syn, s3t):
     except Exception as e:  # reported, not fatal for the headline line
         res["q8_0_b8_error"] = str(e)
     res["attention_microbench_bf16"] = attention_microbench(torch, dev, stream)
+    try:
+        res["encoder_attention_fp16"] = encoder_attention_extras(torch, dev, stream, s3t)
+    except Exception as e:  # reported, not fatal for the headline line
+        res["encoder_attention_error"] = str(e)
     res["rgb8"] = rgb8_extras(torch, dev, stream, trunk, s3t)
     return res
 

@@ -44,6 +44,7 @@ class Oracle:
         L.or_rope_table.argtypes = [C.c_float, C.c_int, _p, _p]
         L.or_rope_axial.argtypes = [_p, _i64, _i64, _p, _p, C.c_float]
         L.or_attention.argtypes = [_p, _p, _p, _i64, _i64, _i64, _i64, C.c_float, _p]
+        L.or_attention_masked.argtypes = [_p, _p, _p, _i64, _i64, _i64, _i64, C.c_float, _p, _p]
         L.or_gelu_erf.argtypes = [_p, _i64, _p]
         L.or_patch_embed.argtypes = [C.c_int, _p, _p, _p]
         L.or_trunk_run.argtypes = [_p, _p, C.c_int, _p, _p]
@@ -114,6 +115,18 @@ class Oracle:
         nq, heads, d = q.shape
         out = np.empty_like(q)
         self.lib.or_attention(_ptr(q), _ptr(k), _ptr(v), nq, k.shape[0], heads, d, scale, _ptr(out))
+        return out
+
+    def attention_masked(self, q, k, v, scale, key_mask=None):
+        """ggml_flash_attn_ext with a per-key additive mask (-inf: key skipped;
+        a row with no key left gives 0).  q [nq][heads][d], k/v [nk][heads][d]."""
+        q = np.ascontiguousarray(q, np.float32)
+        k = np.ascontiguousarray(k, np.float32)
+        v = np.ascontiguousarray(v, np.float32)
+        m = None if key_mask is None else np.ascontiguousarray(key_mask, np.float32)
+        nq, heads, d = q.shape
+        out = np.empty_like(q)
+        self.lib.or_attention_masked(_ptr(q), _ptr(k), _ptr(v), nq, k.shape[0], heads, d, scale, _ptr(m), _ptr(out))
         return out
 
     def gelu_erf(self, x):
@@ -267,6 +280,8 @@ class Reference:
         L.ref_patch_embed.argtypes = [C.c_int, _p, _p, _p, C.c_int]
         if hasattr(L, "ref_bilinear_resize_rgb"):   # absent from the drop-in build
             L.ref_bilinear_resize_rgb.argtypes = [_p, C.c_int, C.c_int, _p]
+        if hasattr(L, "ref_flash_attn_masked"):     # absent from the drop-in build
+            L.ref_flash_attn_masked.argtypes = [_p, _p, _p, _i64, _i64, _i64, _i64, C.c_float, _p, _p, C.c_int]
 
     def _check(self, rc):
         if rc != 0:
@@ -307,6 +322,18 @@ class Reference:
         out = np.empty_like(q)
         self._check(self.lib.ref_flash_attn(_ptr(q), _ptr(k), _ptr(v), q.shape[0], k.shape[0], q.shape[1],
                                             q.shape[2], scale, _ptr(out), n_threads))
+        return out
+
+    def flash_attn_masked(self, q, k, v, scale, key_mask=None, n_threads=4):
+        """ggml_flash_attn_ext with the encoder's F16 mask: key_mask [nk] repeated
+        for every query row (src/encoder_fusion.cpp:120-133)."""
+        q = np.ascontiguousarray(q, np.float32)
+        k = np.ascontiguousarray(k, np.float32)
+        v = np.ascontiguousarray(v, np.float32)
+        m = None if key_mask is None else np.ascontiguousarray(key_mask, np.float32)
+        out = np.empty_like(q)
+        self._check(self.lib.ref_flash_attn_masked(_ptr(q), _ptr(k), _ptr(v), q.shape[0], k.shape[0], q.shape[1],
+                                                   q.shape[2], scale, _ptr(m), _ptr(out), n_threads))
         return out
 
     def gelu_erf(self, x):

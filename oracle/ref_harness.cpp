@@ -173,6 +173,37 @@ int ref_flash_attn(const float * q, const float * k, const float * v, int64_t nq
     return 0;
 }
 
+// ggml_flash_attn_ext, prec F32, with an F16 mask [nq][nk] (ne0 = nk), as
+// mha() of src/encoder_fusion.cpp:63-88 builds it (:120-133, :229).  The mask
+// row is key_mask (f32 [nk], converted to f16) repeated for every query; a
+// null key_mask gives no mask tensor.  Layouts as ref_flash_attn.
+int ref_flash_attn_masked(const float * q, const float * k, const float * v, int64_t nq, int64_t nk,
+                          int64_t heads, int64_t d, float scale, const float * key_mask, float * out,
+                          int n_threads) {
+    const size_t bytes = (size_t) (2 * nq + 2 * nk) * heads * d * 4 + (size_t) nq * nk * 2;
+    Ctx c(bytes * 2 + (size_t) nq * nk * 8 + 64 * 1024 * 1024);
+    ggml_tensor * tq = ggml_new_tensor_4d(c.ctx, GGML_TYPE_F32, d, heads, nq, 1);
+    ggml_tensor * tk = ggml_new_tensor_4d(c.ctx, GGML_TYPE_F32, d, heads, nk, 1);
+    ggml_tensor * tv = ggml_new_tensor_4d(c.ctx, GGML_TYPE_F32, d, heads, nk, 1);
+    std::memcpy(tq->data, q, (size_t) nq * heads * d * 4);
+    std::memcpy(tk->data, k, (size_t) nk * heads * d * 4);
+    std::memcpy(tv->data, v, (size_t) nk * heads * d * 4);
+    ggml_tensor * tm = nullptr;
+    if (key_mask) {
+        tm = ggml_new_tensor_2d(c.ctx, GGML_TYPE_F16, nk, nq);
+        ggml_fp16_t * m = (ggml_fp16_t *) tm->data;
+        for (int64_t i = 0; i < nq; ++i)
+            for (int64_t j = 0; j < nk; ++j) m[i * nk + j] = ggml_fp32_to_fp16(key_mask[j]);
+    }
+    ggml_tensor * r = ggml_flash_attn_ext(c.ctx, ggml_permute(c.ctx, tq, 0, 2, 1, 3),
+                                          ggml_permute(c.ctx, tk, 0, 2, 1, 3),
+                                          ggml_permute(c.ctx, tv, 0, 2, 1, 3), tm, scale, 0.0f, 0.0f);
+    ggml_flash_attn_ext_set_prec(r, GGML_PREC_F32);
+    if (compute(c.ctx, r, n_threads)) return -1;
+    std::memcpy(out, r->data, (size_t) nq * heads * d * 4);
+    return 0;
+}
+
 int ref_gelu_erf(const float * x, int64_t n, float * y) {
     Ctx c((size_t) n * 4 * 3 + 16 * 1024 * 1024);
     ggml_tensor * tx = ggml_new_tensor_1d(c.ctx, GGML_TYPE_F32, n);

@@ -338,6 +338,58 @@ void or_attention(const float *q, const float *k, const float *v, int64_t nq, in
     }
 }
 
+/* ggml_flash_attn_ext, prec F32, with an additive mask that is the same for
+ * every query row: mha() of src/encoder_fusion.cpp:63-88 (head dim 32, scale
+ * 1/sqrt(32)), whose prompt mask (:120-133) repeats one 0 / -inf row.  As in
+ * ggml-cpu/ops.cpp:8254-8271 a key whose mask is -inf is skipped and any other
+ * mask value is added to the scaled score; as in :8353-8354 a row with no
+ * unskipped key (sum 0) comes out as 0.  f32 throughout.  key_mask: [nk] or
+ * NULL.  q: [nq][heads][d], k/v: [nk][heads][d], out: [nq][heads][d]. */
+void or_attention_masked(const float *q, const float *k, const float *v, int64_t nq, int64_t nk,
+                         int64_t heads, int64_t d, float scale, const float *key_mask, float *out) {
+#pragma omp parallel
+    {
+        float *sc = (float *) malloc((size_t) nk * 4);
+        float *acc = (float *) malloc((size_t) d * 4);
+#pragma omp for collapse(2) schedule(static)
+        for (int64_t h = 0; h < heads; h++) {
+            for (int64_t i = 0; i < nq; i++) {
+                const float *qi = q + (i * heads + h) * d;
+                float mx = -INFINITY;
+                for (int64_t j = 0; j < nk; j++) {
+                    const float mv = key_mask ? key_mask[j] : 0.0f;
+                    if (mv == -INFINITY) {
+                        sc[j] = -INFINITY;
+                        continue;
+                    }
+                    const float *kj = k + (j * heads + h) * d;
+                    float s = 0.0f;
+#pragma omp simd reduction(+ : s)
+                    for (int64_t e = 0; e < d; e++) s += qi[e] * kj[e];
+                    s = s * scale + mv;
+                    sc[j] = s;
+                    mx = s > mx ? s : mx;
+                }
+                for (int64_t e = 0; e < d; e++) acc[e] = 0.0f;
+                float sum = 0.0f;
+                for (int64_t j = 0; j < nk; j++) {
+                    if (sc[j] == -INFINITY) continue;
+                    const float p = expf(sc[j] - mx);
+                    sum += p;
+                    const float *vj = v + (j * heads + h) * d;
+#pragma omp simd
+                    for (int64_t e = 0; e < d; e++) acc[e] += p * vj[e];
+                }
+                float *o = out + (i * heads + h) * d;
+                const float inv = sum == 0.0f ? 0.0f : 1.0f / sum;
+                for (int64_t e = 0; e < d; e++) o[e] = acc[e] * inv;
+            }
+        }
+        free(sc);
+        free(acc);
+    }
+}
+
 /* ggml_vec_gelu_erf_f32 (ggml-cpu/vec.h:1018-1023). */
 void or_gelu_erf(const float *x, int64_t n, float *y) {
     const float sqrt_2_inv = 0.70710678118654752440f;

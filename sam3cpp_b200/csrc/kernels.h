@@ -106,6 +106,25 @@ cudaError_t launch_rope_inplace(void* x, int groups, int L, int windowed, int bf
 cudaError_t gemm_prepare();
 cudaError_t attention_prepare();
 
+// Multi-head attention of the encoder fusion (src/encoder_fusion.cpp:63-88):
+// 8 heads of 32 over token-major [len][256] q/k/v, ggml_flash_attn_ext
+// semantics with an optional additive per-key mask.
+struct MhaArgs {
+    const void* q;            // [q_len][256] fp16 / bf16
+    const void* k;            // [kv_len][256]
+    const void* v;            // [kv_len][256]
+    const float* key_mask;    // [kv_len] additive, -inf = key skipped; may be null
+    int q_len;
+    int kv_len;
+    float scale_log2;         // softmax scale * log2(e)
+    int bf16;                 // operand type: fp16 (0) or bf16 (1)
+    int out_f16;              // output fp16/bf16 (1, operand type) or fp32 (0)
+    void* out;                // [q_len][256]
+    int* status;
+};
+cudaError_t launch_mha32(const MhaArgs& a, cudaStream_t stream);
+cudaError_t mha32_prepare();
+
 // Stem weights of a finalized context, for entry points defined outside
 // runtime.cu.  Returns false if the context is null or not finalized.
 struct StemView {

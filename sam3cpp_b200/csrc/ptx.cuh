@@ -287,6 +287,20 @@ S3T_DEV uint64_t umma_desc_sw128(uint32_t smem_addr, uint32_t lbo_bytes, uint32_
     return d;
 }
 
+// Shared-memory matrix descriptor, 64-byte swizzle (tile base 1024-aligned).
+// K-major: rows of 64 B (32 halves), 8-row core groups 512 B apart (SBO).
+// MN-major: rows of 64 B along MN, 8 K-rows per 512 B group (SBO); LBO is
+// the byte distance between 32-element MN chunks.
+S3T_DEV uint64_t umma_desc_sw64(uint32_t smem_addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+    uint64_t d = 0;
+    d |= uint64_t((smem_addr >> 4) & 0x3FFFu);
+    d |= uint64_t((lbo_bytes >> 4) & 0x3FFFu) << 16;
+    d |= uint64_t((sbo_bytes >> 4) & 0x3FFFu) << 32;
+    d |= uint64_t(1) << 46;   // descriptor version (sm_100)
+    d |= uint64_t(4) << 61;   // SWIZZLE_64B
+    return d;
+}
+
 // 32 lanes x 32 consecutive 32-bit columns: thread i of the warp receives
 // row (lane base + i), columns [col, col+32).
 S3T_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {

@@ -105,6 +105,7 @@ int device_state(int device, DeviceState** out) {
         d.num_sms = prop.multiProcessorCount;
         S3T_CUDA(gemm_prepare());
         S3T_CUDA(attention_prepare());
+        S3T_CUDA(mha32_prepare());
         const std::vector<float> rl = rope_table(1.0f, kWindow);
         const std::vector<float> rg = rope_table(float(kWindow) / float(kGrid), kGrid);
         S3T_CUDA(cudaMalloc(&d.rope_local, rl.size() * 4));
@@ -993,6 +994,31 @@ int s3t_attention(int device, const void* q, const void* k, const void* v, int g
     a.out = out;
     a.status = ds->status;
     S3T_CUDA(launch_attention(a, static_cast<cudaStream_t>(stream)));
+    return 0;
+}
+
+int s3t_mha_d32(int device, const void* q, const void* k, const void* v, int q_len, int kv_len,
+                const float* key_mask, void* out, int flags, void* stream) {
+    DeviceState* ds = nullptr;
+    if (device_state(device, &ds)) return -1;
+    S3T_CUDA(cudaSetDevice(device));
+    if (!q || !k || !v || !out) return fail("mha_d32: q, k, v and out must be device pointers");
+    if (q_len <= 0 || kv_len <= 0) return fail("mha_d32 needs q_len > 0 and kv_len > 0");
+    if (flags & ~(S3T_MHA_BF16 | S3T_MHA_OUT_F16)) return fail("mha_d32: unknown flags");
+    if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
+         reinterpret_cast<uintptr_t>(out)) & 15)
+        return fail("mha_d32: q, k, v and out must be 16-byte aligned");
+    MhaArgs a{};
+    a.q = q; a.k = k; a.v = v;
+    a.key_mask = key_mask;
+    a.q_len = q_len; a.kv_len = kv_len;
+    // The reference's scale, 1.0f / std::sqrt(float(kHeadDim)), in the log2 domain.
+    a.scale_log2 = (1.0f / std::sqrt(32.0f)) * 1.4426950408889634f;
+    a.bf16 = (flags & S3T_MHA_BF16) != 0;
+    a.out_f16 = (flags & S3T_MHA_OUT_F16) != 0;
+    a.out = out;
+    a.status = ds->status;
+    S3T_CUDA(launch_mha32(a, static_cast<cudaStream_t>(stream)));
     return 0;
 }
 

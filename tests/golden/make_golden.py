@@ -8,11 +8,16 @@ sam3::VisionTrunk::run for the full-trunk outputs — on seeded inputs.
     python tests/golden/make_golden.py            # op vectors + all three trunks
     python tests/golden/make_golden.py --ops-only
     python tests/golden/make_golden.py --preprocess-only
+    python tests/golden/make_golden.py --mha-only
 
 Files:
   ops.npz                   inputs and ggml outputs of small op cases
   trunk_<fmt>_img0.npz      32-layer output on the seeded <fmt> file and image 0:
                             every STRIDE-th element, plus mean/std of all of it
+  mha_d32.npz               ggml_flash_attn_ext with the encoder fusion's shapes
+                            (8 heads of 32, scale 1/sqrt(32), F16 prompt mask;
+                            src/encoder_fusion.cpp:63-88) on seeded fp16-exact
+                            inputs: MHA_CASES
   preprocess.json           the reference tool's bilinear_resize_rgb
                             (tools/sam3_vision_trunk.cpp:33-66) on seeded uint8
                             images of PREPROCESS_SIZES: sha256 of the fp32
@@ -120,6 +125,45 @@ def op_vectors(ref: Reference) -> dict[str, np.ndarray]:
     return out
 
 
+# (name, q_len, kv_len, mask kind): ragged lengths on both sides, a prompt-like
+# cross attention with padded keys, a single key, a row set with every key
+# masked, and several key blocks with a mask (rescaling across blocks).
+MHA_CASES = [("cross", 150, 33, "prompt"), ("self", 150, 150, None), ("single", 20, 1, None),
+             ("allmasked", 9, 5, "all"), ("long", 64, 200, "prompt")]
+
+
+def mha_inputs(i: int):
+    """Seeded inputs of MHA_CASES[i]: fp16 q [q_len][8][32], k/v [kv_len][8][32]
+    and the fp32 key mask (or None)."""
+    name, nq, nk, kind = MHA_CASES[i]
+    rng = np.random.default_rng(4000 + i)
+    q = (rng.standard_normal((nq, 8, 32)) * 1.5).astype(np.float16)
+    k = (rng.standard_normal((nk, 8, 32)) * 1.5).astype(np.float16)
+    v = rng.standard_normal((nk, 8, 32)).astype(np.float16)
+    mask = None
+    if kind == "prompt":
+        mask = np.zeros(nk, np.float32)
+        mask[rng.random(nk) < 0.3] = -np.inf
+        mask[1] = -0.75          # one finite entry: added to the score
+        mask[0] = 0.0            # at least one key takes part
+    elif kind == "all":
+        mask = np.full(nk, -np.inf, np.float32)
+    return q, k, v, mask
+
+
+def mha_golden(ref: Reference) -> dict[str, np.ndarray]:
+    scale = float(np.float32(1.0) / np.sqrt(np.float32(32.0)))
+    out = {}
+    for i, (name, nq, nk, kind) in enumerate(MHA_CASES):
+        q, k, v, mask = mha_inputs(i)
+        o = ref.flash_attn_masked(q.astype(np.float32), k.astype(np.float32), v.astype(np.float32), scale, mask)
+        out[f"{name}_q"], out[f"{name}_k"], out[f"{name}_v"] = q, k, v
+        if mask is not None:
+            out[f"{name}_mask"] = mask
+        out[f"{name}_out"] = o.astype(np.float32)
+    return out
+
+
 def trunk_golden(ref: Reference, fmt: str, threads: int) -> dict:
     path = s.synthetic_gguf(fmt)
     img = s.synthetic_image(0)
@@ -156,10 +200,15 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ops-only", action="store_true")
     ap.add_argument("--preprocess-only", action="store_true")
+    ap.add_argument("--mha-only", action="store_true")
     ap.add_argument("--formats", default="f16,q8_0,f32")
     ap.add_argument("--threads", type=int, default=8)
     a = ap.parse_args()
     ref = Reference()
+    np.savez_compressed(HERE / "mha_d32.npz", **mha_golden(ref))
+    print("mha_d32.npz written")
+    if a.mha_only:
+        return
     (HERE / "preprocess.json").write_text(json.dumps(preprocess_golden(ref), indent=1))
     print("preprocess.json written")
     if a.preprocess_only:

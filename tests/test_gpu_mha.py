@@ -1,0 +1,128 @@
+"""Parity of the encoder-fusion attention kernel (s3t_mha_d32) through the C ABI.
+
+The reference is mha() of src/encoder_fusion.cpp:63-88: ggml_flash_attn_ext,
+prec F32, 8 heads of 32, scale 1/sqrt(32), with the prompt mask of :120-133
+on the image-to-prompt cross attention.  Checked against the reference's own
+outputs (tests/golden/mha_d32.npz, made by tests/golden/make_golden.py) and,
+at the encoder's full sizes (5184 image tokens), against the oracle.
+
+Tolerance: the kernel takes fp16 (or bf16) q/k/v, accumulates in fp32 and
+rounds P to the operand type, so it is compared within rel-L2 2e-3 (fp16) /
+1e-2 (bf16) and cosine > 0.9999; rows whose keys are all masked must be 0
+exactly, as in ggml's CPU kernel.
+"""
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN, cosine, rel_l2
+
+pytestmark = pytest.mark.gpu
+
+SCALE = float(np.float32(1.0) / np.sqrt(np.float32(32.0)))
+CASES = ["cross", "self", "single", "allmasked", "long"]
+
+
+@pytest.fixture(scope="module")
+def s3t(torch_cuda):
+    import sam3cpp_b200 as s
+    s.lib()
+    return s
+
+
+@pytest.fixture(scope="module")
+def golden():
+    return np.load(GOLDEN / "mha_d32.npz")
+
+
+def _run(s3t, torch, q, k, v, mask, flags=0, out_dtype=None):
+    """q/k/v: host arrays [len][8][32] -> device run -> host fp32 [q_len][8][32]."""
+    dt = torch.bfloat16 if flags & s3t.MHA_BF16 else torch.float16
+    dq, dk, dv = (torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(dt).cuda().reshape(a.shape[0], 256)
+                  for a in (q, k, v))
+    dm = None if mask is None else torch.from_numpy(np.ascontiguousarray(mask, np.float32)).cuda()
+    odt = dt if flags & s3t.MHA_OUT_F16 else torch.float32
+    out = torch.full((q.shape[0], 256), float("nan"), dtype=odt, device="cuda")
+    s3t.mha_d32(0, dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), q.shape[0], k.shape[0],
+                None if dm is None else dm.data_ptr(), out.data_ptr(), flags)
+    torch.cuda.synchronize()
+    assert s3t.lib().s3t_device_status(0) == 0
+    return out.float().cpu().numpy().reshape(q.shape[0], 8, 32)
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_mha_golden(s3t, torch_cuda, golden, case):
+    q, k, v = golden[f"{case}_q"], golden[f"{case}_k"], golden[f"{case}_v"]
+    mask = golden[f"{case}_mask"] if f"{case}_mask" in golden.files else None
+    ref = golden[f"{case}_out"]
+    got = _run(s3t, torch_cuda, q, k, v, mask)
+    assert np.isfinite(got).all()
+    if case == "allmasked":
+        assert np.all(got == 0.0)
+        return
+    assert rel_l2(got, ref) < 2e-3, rel_l2(got, ref)
+    assert cosine(got, ref) > 0.9999
+
+
+def _inputs(seed, nq, nk, scale=1.5):
+    rng = np.random.default_rng(seed)
+    q = (rng.standard_normal((nq, 8, 32)) * scale).astype(np.float16).astype(np.float32)
+    k = (rng.standard_normal((nk, 8, 32)) * scale).astype(np.float16).astype(np.float32)
+    v = rng.standard_normal((nk, 8, 32)).astype(np.float16).astype(np.float32)
+    return q, k, v
+
+
+def test_mha_encoder_self_attention_full(s3t, torch_cuda, oracle):
+    # Self attention of one encoder layer: 72 x 72 image tokens, no mask.
+    # The oracle checks a spread of 320 query rows against all 5184 keys.
+    q, k, v = _inputs(71, 5184, 5184)
+    got = _run(s3t, torch_cuda, q, k, v, None)
+    rows = np.linspace(0, 5183, 320).astype(np.int64)
+    ref = oracle.attention_masked(q[rows], k, v, SCALE, None)
+    assert rel_l2(got[rows], ref) < 2e-3
+    assert cosine(got[rows], ref) > 0.9999
+    assert np.isfinite(got).all()
+
+
+def test_mha_encoder_cross_attention_full(s3t, torch_cuda, oracle):
+    # Image-to-prompt cross attention: 5184 queries, 33 prompt keys, 9 padded.
+    q, k, v = _inputs(72, 5184, 33)
+    mask = np.zeros(33, np.float32)
+    mask[24:] = -np.inf
+    got = _run(s3t, torch_cuda, q, k, v, mask)
+    ref = oracle.attention_masked(q, k, v, SCALE, mask)
+    assert rel_l2(got, ref) < 2e-3
+    assert cosine(got, ref) > 0.9999
+    # Masked keys take no part: changing their values changes nothing.
+    k2, v2 = k.copy(), v.copy()
+    k2[24:] = 7.0
+    v2[24:] = -3.0
+    got2 = _run(s3t, torch_cuda, q, k2, v2, mask)
+    assert np.array_equal(got, got2)
+
+
+def test_mha_bf16_and_f16_output(s3t, torch_cuda, oracle, golden):
+    q, k, v = golden["long_q"].astype(np.float32), golden["long_k"].astype(np.float32), golden["long_v"].astype(np.float32)
+    mask = golden["long_mask"]
+    import torch
+    qb, kb, vb = (torch.from_numpy(a).to(torch.bfloat16).float().numpy() for a in (q, k, v))
+    got = _run(s3t, torch_cuda, qb, kb, vb, mask, flags=s3t.MHA_BF16)
+    ref = oracle.attention_masked(qb, kb, vb, SCALE, mask)
+    assert rel_l2(got, ref) < 1e-2
+    assert cosine(got, ref) > 0.999
+    f32 = _run(s3t, torch_cuda, q, k, v, mask)
+    f16 = _run(s3t, torch_cuda, q, k, v, mask, flags=s3t.MHA_OUT_F16)
+    assert np.array_equal(f16, f32.astype(np.float16).astype(np.float32))
+
+
+def test_mha_rejects_bad_arguments(s3t, torch_cuda):
+    import torch
+    x = torch.zeros((64, 256), dtype=torch.float16, device="cuda")
+    out = torch.zeros((64, 256), dtype=torch.float32, device="cuda")
+    with pytest.raises(s3t.S3TError, match="q_len"):
+        s3t.mha_d32(0, x.data_ptr(), x.data_ptr(), x.data_ptr(), 0, 64, None, out.data_ptr())
+    with pytest.raises(s3t.S3TError, match="aligned"):
+        s3t.mha_d32(0, x.data_ptr() + 2, x.data_ptr(), x.data_ptr(), 64, 64, None, out.data_ptr())
+    with pytest.raises(s3t.S3TError, match="flags"):
+        s3t.mha_d32(0, x.data_ptr(), x.data_ptr(), x.data_ptr(), 64, 64, None, out.data_ptr(), 8)
+    assert s3t.lib().s3t_device_status(0) == 0
