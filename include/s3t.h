@@ -122,19 +122,21 @@ int s3t_attention(int device, const void *q, const void *k, const void *v, int g
  * 256): replaces mha() of src/encoder_fusion.cpp:63-88, the
  * ggml_flash_attn_ext call with prec F32 and scale 1/sqrt(32) that the
  * encoder's self attention (:266, no mask) and image-to-prompt cross
- * attention (:299, prompt mask) run.  q_dev [q_len][256], k_dev/v_dev
- * [kv_len][256] token-major fp16 (flags & S3T_MHA_BF16: bf16), head h in
- * columns [32h, 32h+32).  key_mask_dev: null, or [kv_len] fp32 added to every
- * query row's scaled scores; a key whose entry is -inf takes no part (the
- * reference builds its prompt mask as 0 / -inf rows of this vector,
- * :120-133), and a row whose keys are all masked gives 0, as ggml's CPU
- * kernel does.  out_dev [q_len][256] fp32, or the operand type with
- * S3T_MHA_OUT_F16.  Device pointers, 16-byte aligned, on `device`, enqueued
- * on `stream`.  Returns 0, or -1 with s3t_last_error(). */
+ * attention (:299, prompt mask) run.  `batch` independent sequences (the
+ * reference runs one image per call; batch 1 is that call): q_dev
+ * [batch][q_len][256], k_dev/v_dev [batch][kv_len][256] token-major fp16
+ * (flags & S3T_MHA_BF16: bf16), head h in columns [32h, 32h+32).
+ * key_mask_dev: null, or [batch][kv_len] fp32 added to every query row's
+ * scaled scores; a key whose entry is -inf takes no part (the reference
+ * builds its prompt mask as 0 / -inf rows of this vector, :120-133), and a
+ * row whose keys are all masked gives 0, as ggml's CPU kernel does.  out_dev
+ * [batch][q_len][256] fp32, or the operand type with S3T_MHA_OUT_F16.
+ * Device pointers, 16-byte aligned, on `device`, enqueued on `stream`.
+ * Returns 0, or -1 with s3t_last_error(). */
 #define S3T_MHA_BF16 1
 #define S3T_MHA_OUT_F16 2
-int s3t_mha_d32(int device, const void *q_dev, const void *k_dev, const void *v_dev, int q_len, int kv_len,
-                const float *key_mask_dev, void *out_dev, int flags, void *stream);
+int s3t_mha_d32(int device, const void *q_dev, const void *k_dev, const void *v_dev, int batch, int q_len,
+                int kv_len, const float *key_mask_dev, void *out_dev, int flags, void *stream);
 
 /* The preprocessing of s3t_trunk_run_rgb8 alone: rgb_dev [batch][height]
  * [width][3] uint8 -> out_dev [batch][3][1008][1008] fp32, bit-exact with

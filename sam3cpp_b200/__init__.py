@@ -69,7 +69,7 @@ def lib() -> C.CDLL:
         L.s3t_preprocess_rgb8.argtypes = [i, p, i, i, i, p, p]
         L.s3t_trunk_profile.argtypes = [p, p, i, p, p, C.POINTER(C.c_double), C.POINTER(C.c_int)]
         L.s3t_selftest_wait_timeout.argtypes = [i, i]
-        L.s3t_mha_d32.argtypes = [i, p, p, p, i, i, p, p, i, p]
+        L.s3t_mha_d32.argtypes = [i, p, p, p, i, i, i, p, p, i, p]
         _lib = L
     return _lib
 
@@ -234,16 +234,18 @@ MHA_BF16 = 1
 MHA_OUT_F16 = 2
 
 
-def mha_d32(device: int, q_ptr: int, k_ptr: int, v_ptr: int, q_len: int, kv_len: int, key_mask_ptr: int | None,
-            out_ptr: int, flags: int = 0, stream: int = 0) -> None:
+def mha_d32(device: int, q_ptr: int, k_ptr: int, v_ptr: int, batch: int, q_len: int, kv_len: int,
+            key_mask_ptr: int | None, out_ptr: int, flags: int = 0, stream: int = 0) -> None:
     """Encoder-fusion multi-head attention, 8 heads of 32: mha() of
     src/encoder_fusion.cpp:63-88 (ggml_flash_attn_ext, prec F32, scale 1/sqrt(32)).
 
-    Device pointers: q [q_len][256], k/v [kv_len][256] fp16 (bf16 with MHA_BF16),
-    optional key_mask [kv_len] fp32 added to every row's scaled scores (-inf: key
-    skipped), out [q_len][256] fp32 (operand type with MHA_OUT_F16).  A row whose
-    keys are all masked comes out 0, as in ggml's CPU kernel."""
-    check(lib().s3t_mha_d32(device, C.c_void_p(q_ptr), C.c_void_p(k_ptr), C.c_void_p(v_ptr), q_len, kv_len,
+    `batch` independent sequences back to back.  Device pointers: q
+    [batch][q_len][256], k/v [batch][kv_len][256] fp16 (bf16 with MHA_BF16),
+    optional key_mask [batch][kv_len] fp32 added to every row's scaled scores
+    (-inf: key skipped), out [batch][q_len][256] fp32 (operand type with
+    MHA_OUT_F16).  A row whose keys are all masked comes out 0, as in ggml's
+    CPU kernel."""
+    check(lib().s3t_mha_d32(device, C.c_void_p(q_ptr), C.c_void_p(k_ptr), C.c_void_p(v_ptr), batch, q_len, kv_len,
                             C.c_void_p(key_mask_ptr) if key_mask_ptr else None, C.c_void_p(out_ptr), flags,
                             C.c_void_p(stream) if stream else None))
 

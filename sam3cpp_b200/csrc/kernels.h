@@ -108,18 +108,20 @@ cudaError_t attention_prepare();
 
 // Multi-head attention of the encoder fusion (src/encoder_fusion.cpp:63-88):
 // 8 heads of 32 over token-major [len][256] q/k/v, ggml_flash_attn_ext
-// semantics with an optional additive per-key mask.
+// semantics with an optional additive per-key mask; `batch` independent
+// sequences of the same lengths, back to back.
 struct MhaArgs {
-    const void* q;            // [q_len][256] fp16 / bf16
-    const void* k;            // [kv_len][256]
-    const void* v;            // [kv_len][256]
-    const float* key_mask;    // [kv_len] additive, -inf = key skipped; may be null
+    const void* q;            // [batch][q_len][256] fp16 / bf16
+    const void* k;            // [batch][kv_len][256]
+    const void* v;            // [batch][kv_len][256]
+    const float* key_mask;    // [batch][kv_len] additive, -inf = key skipped; may be null
+    int batch;
     int q_len;
     int kv_len;
     float scale_log2;         // softmax scale * log2(e)
     int bf16;                 // operand type: fp16 (0) or bf16 (1)
     int out_f16;              // output fp16/bf16 (1, operand type) or fp32 (0)
-    void* out;                // [q_len][256]
+    void* out;                // [batch][q_len][256]
     int* status;
 };
 cudaError_t launch_mha32(const MhaArgs& a, cudaStream_t stream);

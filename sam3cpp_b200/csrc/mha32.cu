@@ -12,12 +12,14 @@
 // (:299) has a short, ragged kv_len and the mask.
 //
 // Layout: q/k/v are token-major [len][256] (head h in columns [32h, 32h+32)),
-// exactly the rows the projection GEMMs produce; a 2-D tensor map per operand
-// cuts [rows][32] tiles of one head with 64-byte swizzle.  Output [q_len][256]
-// fp32 (or fp16/bf16), the layout the output projection reads.
+// exactly the rows the projection GEMMs produce, for `batch` sequences back
+// to back; a 3-D tensor map per operand cuts [rows][32] tiles of one head of
+// one sequence with 64-byte swizzle (rows past the sequence's end read as 0).
+// Output [batch][q_len][256] fp32 (or fp16/bf16), the layout the output
+// projection reads.
 //
 // Persistent kernel, same pipeline as the trunk's attention (attention.cu):
-// each CTA walks work items (128-query tile, head).  Warp 0 TMA producer,
+// each CTA walks work items (128-query tile, head, sequence).  Warp 0 TMA producer,
 // warp 1 TMEM owner + UMMA issuer, warps 2..5 softmax + epilogue (one query
 // row per thread).  Per 64-key block b:
 //   S = Q K^T : UMMA M=128 N=64 K=32 (two K steps), TMEM cols [0,64)
@@ -53,13 +55,15 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
 }
 
 struct Item {
-    int qt, head;
+    int qt, head, seq;
 };
 
 __device__ __forceinline__ Item item_of(int w, int n_qt) {
     Item it;
     it.qt = w % n_qt;
-    it.head = w / n_qt;
+    const int r = w / n_qt;
+    it.head = r % kHeadsE;
+    it.seq = r / kHeadsE;
     return it;
 }
 
@@ -89,7 +93,7 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nkv = (a.kv_len + kBKV - 1) / kBKV;
     const int n_qt = (a.q_len + kBQ - 1) / kBQ;
-    const int n_items = n_qt * kHeadsE;
+    const int n_items = n_qt * kHeadsE * a.batch;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < 2; ++i) {
@@ -140,7 +144,7 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
                     break;
                 }
                 mbar_arrive_expect_tx(q_full + qb, kQBytes);
-                tma_load_2d(sQ + qb * kQBytes, &tmQ, q_full + qb, x, it.qt * kBQ);
+                tma_load_3d(sQ + qb * kQBytes, &tmQ, q_full + qb, x, it.qt * kBQ, it.seq);
                 q_armed |= 1u << qb;
                 q_parity = (q_parity & ~(1u << qb)) | (qph << qb);
                 for (int j = 0; j < nkv; ++j, ++b) {
@@ -151,8 +155,8 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
                         break;
                     }
                     mbar_arrive_expect_tx(kv_full + s, 2 * kKVBytes);
-                    tma_load_2d(sK + s * kKVBytes, &tmK, kv_full + s, x, j * kBKV);
-                    tma_load_2d(sV + s * kKVBytes, &tmV, kv_full + s, x, j * kBKV);
+                    tma_load_3d(sK + s * kKVBytes, &tmK, kv_full + s, x, j * kBKV, it.seq);
+                    tma_load_3d(sV + s * kKVBytes, &tmV, kv_full + s, x, j * kBKV, it.seq);
                     armed |= 1u << s;
                     armed_parity = (armed_parity & ~(1u << s)) | (ph << s);
                 }
@@ -254,6 +258,7 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
             const Item it = item_of(w, n_qt);
             const int ob = li & 1;
             const uint32_t tO = tmem + kTmemO + ob * kD;
+            const float* mask_row = any_mask ? a.key_mask + int64_t(it.seq) * a.kv_len : nullptr;
             float m_run = -INFINITY, l_run = 0.f;
             for (int j = 0; j < nkv; ++j, ++b) {
                 if (!mbar_wait(s_full, b & 1, a.status, kErrTimeoutEpilogue, abort_flag)) {
@@ -281,7 +286,7 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
                         const int kk = k0 + c;
                         bool valid = kk < a.kv_len;
                         float mv = 0.f;
-                        if (valid && any_mask) mv = __ldg(a.key_mask + kk);
+                        if (valid && any_mask) mv = __ldg(mask_row + kk);
                         valid = valid && mv != -INFINITY;
                         r[c] = __float_as_uint(valid ? fmaf(__uint_as_float(r[c]), sl2, mv * kLog2e) : -INFINITY);
                     }
@@ -367,7 +372,7 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
                 float v[32];
 #pragma unroll
                 for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(o[i]) * inv;
-                const int64_t off = int64_t(qi) * kModelE + it.head * kD;
+                const int64_t off = (int64_t(it.seq) * a.q_len + qi) * kModelE + it.head * kD;
                 if (a.out_f16) {
                     uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.out) + off);
 #pragma unroll
@@ -400,25 +405,29 @@ cudaError_t mha32_prepare() {
 }
 
 cudaError_t launch_mha32(const MhaArgs& a, cudaStream_t stream) {
-    if (a.q_len <= 0 || a.kv_len <= 0 || !a.q || !a.k || !a.v || !a.out) return cudaErrorInvalidValue;
+    if (a.batch <= 0 || a.q_len <= 0 || a.kv_len <= 0 || !a.q || !a.k || !a.v || !a.out) return cudaErrorInvalidValue;
     // TMA bases and the vector stores of the epilogue need 16-byte alignment.
     if ((reinterpret_cast<uintptr_t>(a.q) | reinterpret_cast<uintptr_t>(a.k) | reinterpret_cast<uintptr_t>(a.v) |
          reinterpret_cast<uintptr_t>(a.out)) & 15)
         return cudaErrorInvalidValue;
     if (reinterpret_cast<uintptr_t>(a.key_mask) & 3) return cudaErrorInvalidValue;
     const CUtensorMapDataType dt = a.bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-    // [len][256] rows; a box is 32 columns (one head, 64 bytes) by 128 or 64 rows.
+    // [batch][len][256]; a box is 32 columns (one head, 64 bytes) by 128 or 64
+    // rows of one sequence.
     CUtensorMap tq, tk, tv;
-    if (!make_tmap_2d(&tq, a.q, dt, 2, kModelE, uint64_t(a.q_len), kD, kBQ, CU_TENSOR_MAP_SWIZZLE_64B))
+    const uint64_t nb = uint64_t(a.batch);
+    if (!make_tmap_3d(&tq, a.q, dt, 2, kModelE, uint64_t(a.q_len), nb, kD, kBQ, CU_TENSOR_MAP_SWIZZLE_64B))
         return cudaErrorInvalidValue;
-    if (!make_tmap_2d(&tk, a.k, dt, 2, kModelE, uint64_t(a.kv_len), kD, kBKV, CU_TENSOR_MAP_SWIZZLE_64B))
+    if (!make_tmap_3d(&tk, a.k, dt, 2, kModelE, uint64_t(a.kv_len), nb, kD, kBKV, CU_TENSOR_MAP_SWIZZLE_64B))
         return cudaErrorInvalidValue;
-    if (!make_tmap_2d(&tv, a.v, dt, 2, kModelE, uint64_t(a.kv_len), kD, kBKV, CU_TENSOR_MAP_SWIZZLE_64B))
+    if (!make_tmap_3d(&tv, a.v, dt, 2, kModelE, uint64_t(a.kv_len), nb, kD, kBKV, CU_TENSOR_MAP_SWIZZLE_64B))
         return cudaErrorInvalidValue;
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int n_items = ((a.q_len + kBQ - 1) / kBQ) * kHeadsE;
+    const int64_t items64 = int64_t((a.q_len + kBQ - 1) / kBQ) * kHeadsE * a.batch;
+    if (items64 > (int64_t(1) << 30)) return cudaErrorInvalidValue;
+    const int n_items = int(items64);
     const int grid = n_items < sms * kCtasPerSm ? n_items : sms * kCtasPerSm;
     if (a.bf16)
         mha32_kernel<1><<<grid, 192, kMhaSmem, stream>>>(tq, tk, tv, a);

@@ -997,13 +997,14 @@ int s3t_attention(int device, const void* q, const void* k, const void* v, int g
     return 0;
 }
 
-int s3t_mha_d32(int device, const void* q, const void* k, const void* v, int q_len, int kv_len,
+int s3t_mha_d32(int device, const void* q, const void* k, const void* v, int batch, int q_len, int kv_len,
                 const float* key_mask, void* out, int flags, void* stream) {
     DeviceState* ds = nullptr;
     if (device_state(device, &ds)) return -1;
     S3T_CUDA(cudaSetDevice(device));
     if (!q || !k || !v || !out) return fail("mha_d32: q, k, v and out must be device pointers");
-    if (q_len <= 0 || kv_len <= 0) return fail("mha_d32 needs q_len > 0 and kv_len > 0");
+    if (batch <= 0 || q_len <= 0 || kv_len <= 0) return fail("mha_d32 needs batch, q_len and kv_len > 0");
+    if (int64_t(batch) * (q_len + 127) / 128 * 8 > (int64_t(1) << 30)) return fail("mha_d32: batch * q_len too large");
     if (flags & ~(S3T_MHA_BF16 | S3T_MHA_OUT_F16)) return fail("mha_d32: unknown flags");
     if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
          reinterpret_cast<uintptr_t>(out)) & 15)
@@ -1011,6 +1012,7 @@ int s3t_mha_d32(int device, const void* q, const void* k, const void* v, int q_l
     MhaArgs a{};
     a.q = q; a.k = k; a.v = v;
     a.key_mask = key_mask;
+    a.batch = batch;
     a.q_len = q_len; a.kv_len = kv_len;
     // The reference's scale, 1.0f / std::sqrt(float(kHeadDim)), in the log2 domain.
     a.scale_log2 = (1.0f / std::sqrt(32.0f)) * 1.4426950408889634f;

@@ -43,7 +43,7 @@ def _run(s3t, torch, q, k, v, mask, flags=0, out_dtype=None):
     dm = None if mask is None else torch.from_numpy(np.ascontiguousarray(mask, np.float32)).cuda()
     odt = dt if flags & s3t.MHA_OUT_F16 else torch.float32
     out = torch.full((q.shape[0], 256), float("nan"), dtype=odt, device="cuda")
-    s3t.mha_d32(0, dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), q.shape[0], k.shape[0],
+    s3t.mha_d32(0, dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), 1, q.shape[0], k.shape[0],
                 None if dm is None else dm.data_ptr(), out.data_ptr(), flags)
     torch.cuda.synchronize()
     assert s3t.lib().s3t_device_status(0) == 0
@@ -115,14 +115,47 @@ def test_mha_bf16_and_f16_output(s3t, torch_cuda, oracle, golden):
     assert np.array_equal(f16, f32.astype(np.float16).astype(np.float32))
 
 
+def test_mha_batched_sequences(s3t, torch_cuda, oracle):
+    # Three sequences in one launch, ragged lengths, a mask row per sequence;
+    # the middle sequence has every key masked (its output must be 0).
+    import torch
+    B, nq, nk = 3, 300, 70
+    rng = np.random.default_rng(73)
+    qs, ks, vs = zip(*(_inputs(80 + b, nq, nk) for b in range(B)))
+    mask = np.zeros((B, nk), np.float32)
+    mask[0, rng.random(nk) < 0.3] = -np.inf
+    mask[0, 0] = 0.0
+    mask[1, :] = -np.inf
+    mask[2, 5] = -1.25
+    dq, dk, dv = (torch.from_numpy(np.stack(a)).half().cuda().reshape(B, -1, 256) for a in (qs, ks, vs))
+    dm = torch.from_numpy(mask).cuda()
+    out = torch.full((B, nq, 256), float("nan"), device="cuda")
+    s3t.mha_d32(0, dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), B, nq, nk, dm.data_ptr(), out.data_ptr())
+    torch.cuda.synchronize()
+    assert s3t.lib().s3t_device_status(0) == 0
+    got = out.cpu().numpy().reshape(B, nq, 8, 32)
+    for b in range(B):
+        ref = oracle.attention_masked(qs[b], ks[b], vs[b], SCALE, mask[b])
+        if b == 1:
+            assert np.all(got[b] == 0.0)
+        else:
+            assert rel_l2(got[b], ref) < 2e-3
+            assert cosine(got[b], ref) > 0.9999
+    # Batched and one-at-a-time launches give the same bits.
+    one = _run(s3t, torch_cuda, qs[2], ks[2], vs[2], mask[2])
+    assert np.array_equal(got[2], one)
+
+
 def test_mha_rejects_bad_arguments(s3t, torch_cuda):
     import torch
     x = torch.zeros((64, 256), dtype=torch.float16, device="cuda")
     out = torch.zeros((64, 256), dtype=torch.float32, device="cuda")
     with pytest.raises(s3t.S3TError, match="q_len"):
-        s3t.mha_d32(0, x.data_ptr(), x.data_ptr(), x.data_ptr(), 0, 64, None, out.data_ptr())
+        s3t.mha_d32(0, x.data_ptr(), x.data_ptr(), x.data_ptr(), 1, 0, 64, None, out.data_ptr())
+    with pytest.raises(s3t.S3TError, match="batch"):
+        s3t.mha_d32(0, x.data_ptr(), x.data_ptr(), x.data_ptr(), 0, 64, 64, None, out.data_ptr())
     with pytest.raises(s3t.S3TError, match="aligned"):
-        s3t.mha_d32(0, x.data_ptr() + 2, x.data_ptr(), x.data_ptr(), 64, 64, None, out.data_ptr())
+        s3t.mha_d32(0, x.data_ptr() + 2, x.data_ptr(), x.data_ptr(), 1, 64, 64, None, out.data_ptr())
     with pytest.raises(s3t.S3TError, match="flags"):
-        s3t.mha_d32(0, x.data_ptr(), x.data_ptr(), x.data_ptr(), 64, 64, None, out.data_ptr(), 8)
+        s3t.mha_d32(0, x.data_ptr(), x.data_ptr(), x.data_ptr(), 1, 64, 64, None, out.data_ptr(), 8)
     assert s3t.lib().s3t_device_status(0) == 0
