@@ -543,7 +543,19 @@ def main():
     ap.add_argument("--images", type=int, default=64)
     ap.add_argument("--no-extras", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--encoder-attention-only", action="store_true",
+                    help="time only the encoder-fusion attention (s3t_mha_d32) and print its numbers")
     a = ap.parse_args()
+    if a.encoder_attention_only:
+        import torch
+        import sam3cpp_b200 as s3t
+        dev = torch.device("cuda", 0)
+        torch.cuda.set_device(dev)
+        stream = torch.cuda.Stream(dev)
+        with torch.cuda.stream(stream):
+            print(json.dumps({"encoder_attention_fp16": encoder_attention_extras(torch, dev, stream, s3t,
+                                                                                 images=a.images)}))
+        return
     if a.warmup < 3 and a.impl == "ours":
         print("note: fewer than 3 warm-up steps", file=sys.stderr)
     if a.impl == "reference":
