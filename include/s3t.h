@@ -135,6 +135,16 @@ int s3t_attention(int device, const void *q, const void *k, const void *v, int g
  * Returns 0, or -1 with s3t_last_error(). */
 #define S3T_MHA_BF16 1
 #define S3T_MHA_OUT_F16 2
+/* With S3T_MHA_BIAS, key_mask_dev is a full additive bias [batch][8][q_len]
+ * [kv_len] fp32 (one row per sequence, head and query): the decoder's image
+ * cross attention with its box relative-position bias (mha() of
+ * src/decoder.cpp:95-127 over image_bias_t, :401-418, :457-465).  The
+ * decoder's other two attentions are the plain call: self attention over its
+ * 201 queries (:430, no mask) and the text cross attention with the prompt
+ * mask row (:443).  The decoder computes softmax explicitly (ggml_soft_max_ext):
+ * the result is the same, except that a row with every key at -inf is NaN
+ * there and 0 here. */
+#define S3T_MHA_BIAS 4
 int s3t_mha_d32(int device, const void *q_dev, const void *k_dev, const void *v_dev, int batch, int q_len,
                 int kv_len, const float *key_mask_dev, void *out_dev, int flags, void *stream);
 

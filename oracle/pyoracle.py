@@ -45,6 +45,7 @@ class Oracle:
         L.or_rope_axial.argtypes = [_p, _i64, _i64, _p, _p, C.c_float]
         L.or_attention.argtypes = [_p, _p, _p, _i64, _i64, _i64, _i64, C.c_float, _p]
         L.or_attention_masked.argtypes = [_p, _p, _p, _i64, _i64, _i64, _i64, C.c_float, _p, _p]
+        L.or_attention_softmax.argtypes = [_p, _p, _p, _i64, _i64, _i64, _i64, C.c_float, _p, _p, _p]
         L.or_gelu_erf.argtypes = [_p, _i64, _p]
         L.or_patch_embed.argtypes = [C.c_int, _p, _p, _p]
         L.or_trunk_run.argtypes = [_p, _p, C.c_int, _p, _p]
@@ -127,6 +128,20 @@ class Oracle:
         nq, heads, d = q.shape
         out = np.empty_like(q)
         self.lib.or_attention_masked(_ptr(q), _ptr(k), _ptr(v), nq, k.shape[0], heads, d, scale, _ptr(m), _ptr(out))
+        return out
+
+    def attention_softmax(self, q, k, v, scale, bias=None, key_mask=None):
+        """The decoder's attention (explicit ggml_soft_max_ext): bias [heads][nq][nk]
+        or key_mask [nk], either optional.  q [nq][heads][d], k/v [nk][heads][d]."""
+        q = np.ascontiguousarray(q, np.float32)
+        k = np.ascontiguousarray(k, np.float32)
+        v = np.ascontiguousarray(v, np.float32)
+        b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+        m = None if key_mask is None else np.ascontiguousarray(key_mask, np.float32)
+        nq, heads, d = q.shape
+        out = np.empty_like(q)
+        self.lib.or_attention_softmax(_ptr(q), _ptr(k), _ptr(v), nq, k.shape[0], heads, d, scale, _ptr(b), _ptr(m),
+                                      _ptr(out))
         return out
 
     def gelu_erf(self, x):
@@ -282,6 +297,8 @@ class Reference:
             L.ref_bilinear_resize_rgb.argtypes = [_p, C.c_int, C.c_int, _p]
         if hasattr(L, "ref_flash_attn_masked"):     # absent from the drop-in build
             L.ref_flash_attn_masked.argtypes = [_p, _p, _p, _i64, _i64, _i64, _i64, C.c_float, _p, _p, C.c_int]
+        if hasattr(L, "ref_decoder_mha"):
+            L.ref_decoder_mha.argtypes = [_p, _p, _p, _i64, _i64, _i64, _i64, C.c_float, _p, _p, _p, C.c_int]
 
     def _check(self, rc):
         if rc != 0:
@@ -334,6 +351,19 @@ class Reference:
         out = np.empty_like(q)
         self._check(self.lib.ref_flash_attn_masked(_ptr(q), _ptr(k), _ptr(v), q.shape[0], k.shape[0], q.shape[1],
                                                    q.shape[2], scale, _ptr(m), _ptr(out), n_threads))
+        return out
+
+    def decoder_mha(self, q, k, v, scale, bias=None, key_mask=None, n_threads=4):
+        """mha() of src/decoder.cpp:95-127 run by ggml: q [nq][heads][d], k/v
+        [nk][heads][d], bias [heads][nq][nk] or key_mask [nk] (F16 prompt mask)."""
+        q = np.ascontiguousarray(q, np.float32)
+        k = np.ascontiguousarray(k, np.float32)
+        v = np.ascontiguousarray(v, np.float32)
+        b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+        m = None if key_mask is None else np.ascontiguousarray(key_mask, np.float32)
+        out = np.empty_like(q)
+        self._check(self.lib.ref_decoder_mha(_ptr(q), _ptr(k), _ptr(v), q.shape[0], k.shape[0], q.shape[1],
+                                             q.shape[2], scale, _ptr(b), _ptr(m), _ptr(out), n_threads))
         return out
 
     def gelu_erf(self, x):

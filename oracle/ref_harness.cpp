@@ -204,6 +204,45 @@ int ref_flash_attn_masked(const float * q, const float * k, const float * v, int
     return 0;
 }
 
+// The decoder's mha() (src/decoder.cpp:95-127) as a ggml graph: the same
+// views, ggml_mul_mat for the scores, ggml_soft_max_ext with the mask and
+// ggml_mul_mat with the transposed V.  bias: F32 [heads][nq][nk] as
+// image_bias_t (:418); key_mask: [nk] written as the F16 prompt mask rows
+// (:131-143, :414).  q: [nq][heads*d], k/v: [nk][heads*d]; out [nq][heads*d].
+int ref_decoder_mha(const float * q, const float * k, const float * v, int64_t nq, int64_t nk, int64_t heads,
+                    int64_t d, float scale, const float * bias, const float * key_mask, float * out,
+                    int n_threads) {
+    const size_t bytes = (size_t) (2 * nq + 2 * nk) * heads * d * 4 + (size_t) nq * nk * heads * 4 * 4;
+    Ctx c(bytes * 3 + 64 * 1024 * 1024);
+    ggml_tensor * tq = ggml_new_tensor_2d(c.ctx, GGML_TYPE_F32, heads * d, nq);
+    ggml_tensor * tk = ggml_new_tensor_2d(c.ctx, GGML_TYPE_F32, heads * d, nk);
+    ggml_tensor * tv = ggml_new_tensor_2d(c.ctx, GGML_TYPE_F32, heads * d, nk);
+    std::memcpy(tq->data, q, (size_t) nq * heads * d * 4);
+    std::memcpy(tk->data, k, (size_t) nk * heads * d * 4);
+    std::memcpy(tv->data, v, (size_t) nk * heads * d * 4);
+    ggml_tensor * tm = nullptr;
+    if (bias) {
+        tm = ggml_new_tensor_3d(c.ctx, GGML_TYPE_F32, nk, nq, heads);
+        std::memcpy(tm->data, bias, (size_t) nk * nq * heads * 4);
+    } else if (key_mask) {
+        tm = ggml_new_tensor_2d(c.ctx, GGML_TYPE_F16, nk, nq);
+        ggml_fp16_t * m = (ggml_fp16_t *) tm->data;
+        for (int64_t i = 0; i < nq; ++i)
+            for (int64_t j = 0; j < nk; ++j) m[i * nk + j] = ggml_fp32_to_fp16(key_mask[j]);
+    }
+    ggml_tensor * qh = ggml_permute(c.ctx, ggml_cont_3d(c.ctx, tq, d, heads, nq), 0, 2, 1, 3);
+    ggml_tensor * kh = ggml_permute(c.ctx, ggml_cont_3d(c.ctx, tk, d, heads, nk), 0, 2, 1, 3);
+    ggml_tensor * vh = ggml_cont_3d(c.ctx, ggml_permute(c.ctx, ggml_cont_3d(c.ctx, tv, d, heads, nk), 1, 2, 0, 3),
+                                    nk, d, heads);
+    ggml_tensor * scores = ggml_mul_mat(c.ctx, kh, qh);
+    ggml_tensor * probs = ggml_soft_max_ext(c.ctx, scores, tm, scale, 0.0f);
+    ggml_tensor * attn = ggml_mul_mat(c.ctx, vh, probs);
+    ggml_tensor * r = ggml_cont_2d(c.ctx, ggml_permute(c.ctx, attn, 0, 2, 1, 3), heads * d, nq);
+    if (compute(c.ctx, r, n_threads)) return -1;
+    std::memcpy(out, r->data, (size_t) nq * heads * d * 4);
+    return 0;
+}
+
 int ref_gelu_erf(const float * x, int64_t n, float * y) {
     Ctx c((size_t) n * 4 * 3 + 16 * 1024 * 1024);
     ggml_tensor * tx = ggml_new_tensor_1d(c.ctx, GGML_TYPE_F32, n);

@@ -390,6 +390,56 @@ void or_attention_masked(const float *q, const float *k, const float *v, int64_t
     }
 }
 
+/* The decoder's attention, mha() of src/decoder.cpp:95-127: scores = k.q per
+ * head (ggml_mul_mat, f32 dots), ggml_soft_max_ext(scores, mask, scale) and
+ * probs.v (ggml_mul_mat).  The softmax follows ggml-cpu/ops.cpp:5284-5330:
+ * w = s*scale + mask, m = max w, p = expf(w - m) summed in double, p *= 1/sum
+ * (so a row with every entry -inf is NaN, as there).  The mask is either a full
+ * bias [heads][nq][nk] (the image cross attention's box relative-position
+ * bias, :401-418, :457-465) or one row [nk] repeated for every query (the text
+ * cross attention's prompt mask, :131-143, :443-451); either may be NULL.
+ * q: [nq][heads][d], k/v: [nk][heads][d], out: [nq][heads][d]. */
+void or_attention_softmax(const float *q, const float *k, const float *v, int64_t nq, int64_t nk,
+                          int64_t heads, int64_t d, float scale, const float *bias, const float *key_mask,
+                          float *out) {
+#pragma omp parallel
+    {
+        float *w = (float *) malloc((size_t) nk * 4);
+#pragma omp for collapse(2) schedule(static)
+        for (int64_t h = 0; h < heads; h++) {
+            for (int64_t i = 0; i < nq; i++) {
+                const float *qi = q + (i * heads + h) * d;
+                const float *brow = bias ? bias + (h * nq + i) * nk : NULL;
+                float mx = -INFINITY;
+                for (int64_t j = 0; j < nk; j++) {
+                    const float *kj = k + (j * heads + h) * d;
+                    float s = 0.0f;
+                    for (int64_t e = 0; e < d; e++) s += qi[e] * kj[e];
+                    s *= scale;
+                    if (brow) s += brow[j];
+                    if (key_mask) s += key_mask[j];
+                    w[j] = s;
+                    mx = s > mx ? s : mx;
+                }
+                double sum = 0.0;
+                for (int64_t j = 0; j < nk; j++) {
+                    w[j] = expf(w[j] - mx);
+                    sum += (double) w[j];
+                }
+                const float inv = (float) (1.0 / sum);
+                float *o = out + (i * heads + h) * d;
+                for (int64_t e = 0; e < d; e++) o[e] = 0.0f;
+                for (int64_t j = 0; j < nk; j++) {
+                    const float p = w[j] * inv;
+                    const float *vj = v + (j * heads + h) * d;
+                    for (int64_t e = 0; e < d; e++) o[e] += p * vj[e];
+                }
+            }
+        }
+        free(w);
+    }
+}
+
 /* ggml_vec_gelu_erf_f32 (ggml-cpu/vec.h:1018-1023). */
 void or_gelu_erf(const float *x, int64_t n, float *y) {
     const float sqrt_2_inv = 0.70710678118654752440f;

@@ -38,6 +38,9 @@ void or_attention(const float *q, const float *k, const float *v, int64_t nq, in
                   int64_t heads, int64_t d, float scale, float *out);
 void or_attention_masked(const float *q, const float *k, const float *v, int64_t nq, int64_t nk,
                          int64_t heads, int64_t d, float scale, const float *key_mask, float *out);
+void or_attention_softmax(const float *q, const float *k, const float *v, int64_t nq, int64_t nk,
+                          int64_t heads, int64_t d, float scale, const float *bias, const float *key_mask,
+                          float *out);
 void or_gelu_erf(const float *x, int64_t n, float *y);
 void or_patch_embed(int wtype, const void *w, const float *image, float *out);
 /* uint8 RGB (h x w x 3) -> normalized [3][1008][1008] fp32, the reference's

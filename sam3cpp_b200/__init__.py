@@ -232,6 +232,7 @@ class VisionTrunk:
 
 MHA_BF16 = 1
 MHA_OUT_F16 = 2
+MHA_BIAS = 4     # key_mask is a full bias [batch][8][q_len][kv_len] (the decoder's image cross attention)
 
 
 def mha_d32(device: int, q_ptr: int, k_ptr: int, v_ptr: int, batch: int, q_len: int, kv_len: int,

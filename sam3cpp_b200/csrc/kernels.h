@@ -114,13 +114,15 @@ struct MhaArgs {
     const void* q;            // [batch][q_len][256] fp16 / bf16
     const void* k;            // [batch][kv_len][256]
     const void* v;            // [batch][kv_len][256]
-    const float* key_mask;    // [batch][kv_len] additive, -inf = key skipped; may be null
+    const float* key_mask;    // [batch][kv_len] additive, -inf = key skipped; may be null;
+                              // with `bias`: [batch][8 heads][q_len][kv_len]
     int batch;
     int q_len;
     int kv_len;
     float scale_log2;         // softmax scale * log2(e)
     int bf16;                 // operand type: fp16 (0) or bf16 (1)
     int out_f16;              // output fp16/bf16 (1, operand type) or fp32 (0)
+    int bias;                 // key_mask holds one row per (sequence, head, query)
     void* out;                // [batch][q_len][256]
     int* status;
 };

@@ -26,8 +26,11 @@
 //   P = 2^(S*scale*log2e + mask*log2e - m) -> TMEM P[b & 1] (32 columns)
 //   O += P V  : UMMA M=128 N=32 K=64, A = P from TMEM, V MN-major, into
 //               O[item & 1] (32 columns)
-// Keys past kv_len (the last, ragged block) are masked like -inf mask
-// entries; query rows past q_len run on zero-filled Q rows and are not
+// The mask may instead be a full additive bias per (sequence, head, query,
+// key): the decoder's box relative-position bias on its image cross attention
+// (src/decoder.cpp:401-418, :457-465), read row by row by the thread that owns
+// the query.  Keys past kv_len (the last, ragged block) are masked like -inf
+// mask entries; query rows past q_len run on zero-filled Q rows and are not
 // stored.  TMEM: S 64 + O 2x32 + P 2x32 = 192 of the 256 columns allocated,
 // two CTAs per SM.
 #include <math.h>
@@ -258,7 +261,14 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
             const Item it = item_of(w, n_qt);
             const int ob = li & 1;
             const uint32_t tO = tmem + kTmemO + ob * kD;
-            const float* mask_row = any_mask ? a.key_mask + int64_t(it.seq) * a.kv_len : nullptr;
+            const float* mask_row = nullptr;
+            if (any_mask && a.bias) {
+                // Query rows past q_len are computed but never stored; they read the last row.
+                const int qi = min(it.qt * kBQ + row, a.q_len - 1);
+                mask_row = a.key_mask + ((int64_t(it.seq) * kHeadsE + it.head) * a.q_len + qi) * a.kv_len;
+            } else if (any_mask) {
+                mask_row = a.key_mask + int64_t(it.seq) * a.kv_len;
+            }
             float m_run = -INFINITY, l_run = 0.f;
             for (int j = 0; j < nkv; ++j, ++b) {
                 if (!mbar_wait(s_full, b & 1, a.status, kErrTimeoutEpilogue, abort_flag)) {

@@ -1005,7 +1005,8 @@ int s3t_mha_d32(int device, const void* q, const void* k, const void* v, int bat
     if (!q || !k || !v || !out) return fail("mha_d32: q, k, v and out must be device pointers");
     if (batch <= 0 || q_len <= 0 || kv_len <= 0) return fail("mha_d32 needs batch, q_len and kv_len > 0");
     if (int64_t(batch) * (q_len + 127) / 128 * 8 > (int64_t(1) << 30)) return fail("mha_d32: batch * q_len too large");
-    if (flags & ~(S3T_MHA_BF16 | S3T_MHA_OUT_F16)) return fail("mha_d32: unknown flags");
+    if (flags & ~(S3T_MHA_BF16 | S3T_MHA_OUT_F16 | S3T_MHA_BIAS)) return fail("mha_d32: unknown flags");
+    if ((flags & S3T_MHA_BIAS) && !key_mask) return fail("mha_d32: S3T_MHA_BIAS needs the bias array");
     if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
          reinterpret_cast<uintptr_t>(out)) & 15)
         return fail("mha_d32: q, k, v and out must be 16-byte aligned");
@@ -1018,6 +1019,7 @@ int s3t_mha_d32(int device, const void* q, const void* k, const void* v, int bat
     a.scale_log2 = (1.0f / std::sqrt(32.0f)) * 1.4426950408889634f;
     a.bf16 = (flags & S3T_MHA_BF16) != 0;
     a.out_f16 = (flags & S3T_MHA_OUT_F16) != 0;
+    a.bias = (flags & S3T_MHA_BIAS) != 0;
     a.out = out;
     a.status = ds->status;
     S3T_CUDA(launch_mha32(a, static_cast<cudaStream_t>(stream)));

@@ -18,6 +18,9 @@ Files:
                             (8 heads of 32, scale 1/sqrt(32), F16 prompt mask;
                             src/encoder_fusion.cpp:63-88) on seeded fp16-exact
                             inputs: MHA_CASES
+  mha_d32_decoder.npz       mha() of src/decoder.cpp:95-127 (mul_mat, soft_max_ext
+                            with the prompt mask or the box bias, mul_mat) run by
+                            ggml on seeded fp16-exact inputs: DECODER_CASES
   preprocess.json           the reference tool's bilinear_resize_rgb
                             (tools/sam3_vision_trunk.cpp:33-66) on seeded uint8
                             images of PREPROCESS_SIZES: sha256 of the fp32
@@ -151,6 +154,45 @@ def mha_inputs(i: int):
     return q, k, v, mask
 
 
+# The decoder's three attentions at its 201 queries: self attention, the text
+# cross attention with a padded prompt, and the image cross attention with a
+# full [8][201][kv] relative-position bias (fewer keys than 5184 to keep the
+# file small; the GPU tests run 5184 against the oracle).
+DECODER_CASES = [("dec_self", 201, 201, None), ("dec_text", 201, 33, "prompt"), ("dec_image", 201, 70, "bias")]
+
+
+def decoder_inputs(i: int):
+    name, nq, nk, kind = DECODER_CASES[i]
+    rng = np.random.default_rng(4100 + i)
+    q = (rng.standard_normal((nq, 8, 32)) * 1.5).astype(np.float16)
+    k = (rng.standard_normal((nk, 8, 32)) * 1.5).astype(np.float16)
+    v = rng.standard_normal((nk, 8, 32)).astype(np.float16)
+    mask = bias = None
+    if kind == "prompt":
+        mask = np.zeros(nk, np.float32)
+        mask[24:] = -np.inf
+    elif kind == "bias":
+        bias = (rng.standard_normal((8, nq, nk)) * 2.0).astype(np.float32)
+        bias[:, :, 3] = -np.inf      # a key no query of any head may use
+    return q, k, v, mask, bias
+
+
+def decoder_golden(ref: Reference) -> dict[str, np.ndarray]:
+    scale = float(np.float32(1.0) / np.sqrt(np.float32(32.0)))
+    out = {}
+    for i, (name, nq, nk, kind) in enumerate(DECODER_CASES):
+        q, k, v, mask, bias = decoder_inputs(i)
+        o = ref.decoder_mha(q.astype(np.float32), k.astype(np.float32), v.astype(np.float32), scale, bias=bias,
+                            key_mask=mask)
+        out[f"{name}_q"], out[f"{name}_k"], out[f"{name}_v"] = q, k, v
+        if mask is not None:
+            out[f"{name}_mask"] = mask
+        if bias is not None:
+            out[f"{name}_bias"] = bias
+        out[f"{name}_out"] = o.astype(np.float32)
+    return out
+
+
 def mha_golden(ref: Reference) -> dict[str, np.ndarray]:
     scale = float(np.float32(1.0) / np.sqrt(np.float32(32.0)))
     out = {}
@@ -206,7 +248,8 @@ def main():
     a = ap.parse_args()
     ref = Reference()
     np.savez_compressed(HERE / "mha_d32.npz", **mha_golden(ref))
-    print("mha_d32.npz written")
+    np.savez_compressed(HERE / "mha_d32_decoder.npz", **decoder_golden(ref))
+    print("mha_d32.npz, mha_d32_decoder.npz written")
     if a.mha_only:
         return
     (HERE / "preprocess.json").write_text(json.dumps(preprocess_golden(ref), indent=1))

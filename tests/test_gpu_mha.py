@@ -2,9 +2,13 @@
 
 The reference is mha() of src/encoder_fusion.cpp:63-88: ggml_flash_attn_ext,
 prec F32, 8 heads of 32, scale 1/sqrt(32), with the prompt mask of :120-133
-on the image-to-prompt cross attention.  Checked against the reference's own
-outputs (tests/golden/mha_d32.npz, made by tests/golden/make_golden.py) and,
-at the encoder's full sizes (5184 image tokens), against the oracle.
+on the image-to-prompt cross attention; and mha() of src/decoder.cpp:95-127
+(ggml_mul_mat + ggml_soft_max_ext) for the decoder's self, text and image
+cross attention, the last with a full box relative-position bias
+(S3T_MHA_BIAS).  Checked against the reference's own outputs
+(tests/golden/mha_d32.npz, mha_d32_decoder.npz, made by
+tests/golden/make_golden.py) and, at full sizes (5184 image tokens), against
+the oracle.
 
 Tolerance: the kernel takes fp16 (or bf16) q/k/v, accumulates in fp32 and
 rounds P to the operand type, so it is compared within rel-L2 2e-3 (fp16) /
@@ -146,6 +150,44 @@ def test_mha_batched_sequences(s3t, torch_cuda, oracle):
     assert np.array_equal(got[2], one)
 
 
+def _run_bias(s3t, torch, q, k, v, bias):
+    dq, dk, dv = (torch.from_numpy(np.ascontiguousarray(a, np.float32)).half().cuda().reshape(a.shape[0], 256)
+                  for a in (q, k, v))
+    db = torch.from_numpy(np.ascontiguousarray(bias, np.float32)).cuda()
+    out = torch.full((q.shape[0], 256), float("nan"), device="cuda")
+    s3t.mha_d32(0, dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), 1, q.shape[0], k.shape[0], db.data_ptr(),
+                out.data_ptr(), s3t.MHA_BIAS)
+    torch.cuda.synchronize()
+    assert s3t.lib().s3t_device_status(0) == 0
+    return out.cpu().numpy().reshape(q.shape[0], 8, 32)
+
+
+@pytest.mark.parametrize("case", ["dec_self", "dec_text", "dec_image"])
+def test_mha_decoder_golden(s3t, torch_cuda, case):
+    g = np.load(GOLDEN / "mha_d32_decoder.npz")
+    q, k, v, ref = g[f"{case}_q"], g[f"{case}_k"], g[f"{case}_v"], g[f"{case}_out"]
+    if f"{case}_bias" in g.files:
+        got = _run_bias(s3t, torch_cuda, q, k, v, g[f"{case}_bias"])
+    else:
+        got = _run(s3t, torch_cuda, q, k, v, g[f"{case}_mask"] if f"{case}_mask" in g.files else None)
+    assert np.isfinite(got).all()
+    assert rel_l2(got, ref) < 2e-3, rel_l2(got, ref)
+    assert cosine(got, ref) > 0.9999
+
+
+def test_mha_decoder_image_cross_attention_full(s3t, torch_cuda, oracle):
+    # The decoder's 201 queries against the 5184 image tokens with a bias per
+    # head, query and key; some bias entries are -inf (keys that take no part).
+    q, k, v = _inputs(74, 201, 5184)
+    rng = np.random.default_rng(75)
+    bias = (rng.standard_normal((8, 201, 5184)) * 2.0).astype(np.float32)
+    bias[rng.random(bias.shape) < 0.05] = -np.inf
+    got = _run_bias(s3t, torch_cuda, q, k, v, bias)
+    ref = oracle.attention_softmax(q, k, v, SCALE, bias=bias)
+    assert rel_l2(got, ref) < 2e-3
+    assert cosine(got, ref) > 0.9999
+
+
 def test_mha_rejects_bad_arguments(s3t, torch_cuda):
     import torch
     x = torch.zeros((64, 256), dtype=torch.float16, device="cuda")
@@ -158,4 +200,6 @@ def test_mha_rejects_bad_arguments(s3t, torch_cuda):
         s3t.mha_d32(0, x.data_ptr() + 2, x.data_ptr(), x.data_ptr(), 1, 64, 64, None, out.data_ptr())
     with pytest.raises(s3t.S3TError, match="flags"):
         s3t.mha_d32(0, x.data_ptr(), x.data_ptr(), x.data_ptr(), 1, 64, 64, None, out.data_ptr(), 8)
+    with pytest.raises(s3t.S3TError, match="BIAS"):
+        s3t.mha_d32(0, x.data_ptr(), x.data_ptr(), x.data_ptr(), 1, 64, 64, None, out.data_ptr(), s3t.MHA_BIAS)
     assert s3t.lib().s3t_device_status(0) == 0
