@@ -345,11 +345,13 @@ def attention_microbench(torch, dev, stream, images=32):
 
 
 def encoder_attention_extras(torch, dev, stream, s3t, images=4):
-    """The encoder fusion's attention (s3t_mha_d32: 8 heads of 32): self
-    attention over the 72x72 image tokens of `images` images (one batched
-    launch, no mask; and one launch per image, the reference's batch of 1) and
-    image-to-prompt cross attention (5184 queries, 33 prompt keys of which 9
-    are masked).  fp16 q/k/v ~ N(0, 1.5^2), seed 6."""
+    """The encoder fusion's and decoder's attention (s3t_mha_d32: 8 heads of
+    32): encoder self attention over the 72x72 image tokens of `images` images
+    (one batched launch, no mask; and one launch per image, the reference's
+    batch of 1), image-to-prompt cross attention (5184 queries, 33 prompt keys
+    of which 9 are masked), and the decoder's self attention (201 queries) and
+    image cross attention (201 x 5184 with a full box bias).  fp16 q/k/v ~
+    N(0, 1.5^2), bias ~ N(0, 2^2), seed 6."""
     peak = measured_peaks()[0]
     g = torch.Generator(device=dev).manual_seed(6)
     T = 5184
@@ -373,16 +375,35 @@ def encoder_attention_extras(torch, dev, stream, s3t, images=4):
         s3t.mha_d32(dev.index, q[0].data_ptr(), kp.data_ptr(), vp.data_ptr(), 1, T, 33, mask.data_ptr(),
                     op.data_ptr(), 0, sp)
 
+    # The decoder's 201 queries: self attention, and the image cross attention
+    # against the 5184 tokens with a full [8][201][5184] box bias (S3T_MHA_BIAS).
+    NQ = 201
+    dq = (torch.randn((NQ, 256), generator=g, device=dev) * 1.5).half()
+    bias = torch.randn((8, NQ, T), generator=g, device=dev) * 2.0
+
+    def dec_self():
+        s3t.mha_d32(dev.index, dq.data_ptr(), dq.data_ptr(), dq.data_ptr(), 1, NQ, NQ, None, op.data_ptr(), 0, sp)
+
+    def dec_image():
+        s3t.mha_d32(dev.index, dq.data_ptr(), k[0].data_ptr(), v[0].data_ptr(), 1, NQ, T, bias.data_ptr(),
+                    op.data_ptr(), s3t.MHA_BIAS, sp)
+
     ms_self = _event_ms(torch, dev, stream, self_attn, 3, 10)
     ms_one = _event_ms(torch, dev, stream, self_attn_per_image, 3, 10)
     ms_cross = _event_ms(torch, dev, stream, cross_attn, 3, 20)
+    ms_dec_self = _event_ms(torch, dev, stream, dec_self, 3, 20)
+    ms_dec_image = _event_ms(torch, dev, stream, dec_image, 3, 20)
     check_status = s3t.lib().s3t_device_status(dev.index)
     flop = 4.0 * images * T * T * 32 * 8
     tf = flop / (ms_self / 1e3) / 1e12
     return {"self_shape": f"{images}x{T}x{T}x8x32", "self_ms": round(ms_self, 4), "self_tflops": round(tf, 1),
             "self_frac_of_bf16_peak": round(tf / peak, 4),
             "self_one_launch_per_image_tflops": round(flop / (ms_one / 1e3) / 1e12, 1),
-            "cross_shape": f"{T}x33(9 masked)x8x32", "cross_ms": round(ms_cross, 4), "status": check_status}
+            "cross_shape": f"{T}x33(9 masked)x8x32", "cross_ms": round(ms_cross, 4),
+            "decoder_self_shape": f"{NQ}x{NQ}x8x32", "decoder_self_ms": round(ms_dec_self, 4),
+            "decoder_image_shape": f"{NQ}x{T}x8x32 + bias", "decoder_image_ms": round(ms_dec_image, 4),
+            "decoder_image_tflops": round(4.0 * NQ * T * 32 * 8 / (ms_dec_image / 1e3) / 1e12, 1),
+            "status": check_status}
 
 
 def config_extras(torch, dev, stream, trunk, syn, s3t):

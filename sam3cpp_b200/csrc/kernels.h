@@ -123,6 +123,9 @@ struct MhaArgs {
     int bf16;                 // operand type: fp16 (0) or bf16 (1)
     int out_f16;              // output fp16/bf16 (1, operand type) or fp32 (0)
     int bias;                 // key_mask holds one row per (sequence, head, query)
+    int splits;               // key-range splits per (query tile, head, sequence); 1 = direct output
+    float* ws_o;              // splits > 1: unnormalised O partials [items][128][splits][32]
+    float* ws_ml;             // splits > 1: (m, l) of each partial
     void* out;                // [batch][q_len][256]
     int* status;
 };

@@ -19,7 +19,11 @@
 // projection reads.
 //
 // Persistent kernel, same pipeline as the trunk's attention (attention.cu):
-// each CTA walks work items (128-query tile, head, sequence).  Warp 0 TMA producer,
+// each CTA walks work items (128-query tile, head, sequence, key range).  When
+// the query tiles are too few to fill the GPU (the decoder's 201 queries
+// against 5184 image tokens make 16 tiles), the key blocks of a tile are split
+// into ranges: each item then writes its unnormalised O with its (m, l) to a
+// scratch buffer, and mha32_combine merges the ranges per row.  Warp 0 TMA producer,
 // warp 1 TMEM owner + UMMA issuer, warps 2..5 softmax + epilogue (one query
 // row per thread).  Per 64-key block b:
 //   S = Q K^T : UMMA M=128 N=64 K=32 (two K steps), TMEM cols [0,64)
@@ -58,19 +62,32 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
 }
 
 struct Item {
-    int qt, head, seq;
+    int qt, head, seq, split;
+    int j0, j1;   // key blocks [j0, j1) of this item
 };
 
-__device__ __forceinline__ Item item_of(int w, int n_qt) {
+__device__ __forceinline__ Item item_of(int w, int n_qt, int splits, int nkv) {
     Item it;
-    it.qt = w % n_qt;
-    const int r = w / n_qt;
+    it.split = w % splits;
+    const int w2 = w / splits;
+    it.qt = w2 % n_qt;
+    const int r = w2 / n_qt;
     it.head = r % kHeadsE;
     it.seq = r / kHeadsE;
+    it.j0 = int(int64_t(it.split) * nkv / splits);
+    it.j1 = int(int64_t(it.split + 1) * nkv / splits);
     return it;
 }
 
-template <int BF16>
+// Index of a row's partial in the scratch buffers (splits > 1).
+__device__ __forceinline__ int64_t partial_index(int seq, int head, int qt, int row, int split, int n_qt,
+                                                 int splits) {
+    return (int64_t((seq * kHeadsE + head) * n_qt + qt) * kBQ + row) * splits + split;
+}
+
+// MASK: a mask or bias array was given (compiled apart, so the unmasked
+// self attention keeps its registers for the softmax).
+template <int BF16, bool MASK>
 __global__ void __launch_bounds__(192, kCtasPerSm)
     mha32_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                  const __grid_constant__ CUtensorMap tmV, const MhaArgs a) {
@@ -96,7 +113,8 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nkv = (a.kv_len + kBKV - 1) / kBKV;
     const int n_qt = (a.q_len + kBQ - 1) / kBQ;
-    const int n_items = n_qt * kHeadsE * a.batch;
+    const int splits = a.splits;
+    const int n_items = n_qt * kHeadsE * a.batch * splits;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < 2; ++i) {
@@ -138,7 +156,7 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
             int b = 0;   // global block counter of this CTA
             int li = 0;  // local item counter
             for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++li) {
-                const Item it = item_of(w, n_qt);
+                const Item it = item_of(w, n_qt, splits, nkv);
                 const int x = it.head * kD;   // column of this head: 64-byte aligned
                 const int qb = li & 1;
                 const uint32_t qph = (li >> 1) & 1;
@@ -150,7 +168,7 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
                 tma_load_3d(sQ + qb * kQBytes, &tmQ, q_full + qb, x, it.qt * kBQ, it.seq);
                 q_armed |= 1u << qb;
                 q_parity = (q_parity & ~(1u << qb)) | (qph << qb);
-                for (int j = 0; j < nkv; ++j, ++b) {
+                for (int j = it.j0; j < it.j1; ++j, ++b) {
                     const int s = b % kKVStages;
                     const uint32_t ph = (b / kKVStages) & 1;
                     if (!mbar_wait(kv_empty + s, ph ^ 1, a.status, kErrTimeoutProducer, abort_flag)) {
@@ -178,8 +196,15 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
         if (lane == 0) {
             constexpr uint32_t idS = umma_idesc_f16(kBQ, kBKV, BF16, 0);
             constexpr uint32_t idO = umma_idesc_f16(kBQ, kD, BF16, 1);
-            const int my_items = int(blockIdx.x) < n_items ? (n_items - 1 - int(blockIdx.x)) / int(gridDim.x) + 1 : 0;
-            const int total = my_items * nkv;
+            // Key blocks of this CTA's li-th item, and of all its items.
+            auto count_of = [&](int li_) -> int {
+                const int w = int(blockIdx.x) + li_ * int(gridDim.x);
+                if (w >= n_items) return 0;
+                const Item it = item_of(w, n_qt, splits, nkv);
+                return it.j1 - it.j0;
+            };
+            int total = 0;
+            for (int w = blockIdx.x, li_ = 0; w < n_items; w += gridDim.x, ++li_) total += count_of(li_);
             bool ok = true, issued = false;
             // Descriptors are built once.  A K step of 16 advances the start
             // address field by 32 bytes (2) for the K-major Q and K tiles, and
@@ -190,7 +215,7 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
             const uint64_t dV0 = umma_desc_sw64(smem_u32(sV), kKVBytes, 512);
             constexpr uint64_t kStageStep = kKVBytes >> 4;
             // State of the next S block to issue (block counter, key block, item, ring stage/phase).
-            int sb = 0, sj = 0, sli = 0, ss = 0;
+            int sb = 0, sj = 0, sli = 0, ss = 0, scnt = count_of(0);
             uint32_t sph = 0;
             auto issue_s = [&]() -> bool {
                 const int qb = sli & 1;
@@ -203,15 +228,15 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
 #pragma unroll
                 for (int k = 0; k < kD / 16; ++k) umma_f16_ss(tS, dq + 2 * k, dk + 2 * k, idS, k != 0);
                 umma_commit(s_full);
-                if (sj == nkv - 1) umma_commit(q_empty + qb);   // Q buffer reusable once these S complete
+                if (sj == scnt - 1) umma_commit(q_empty + qb);   // Q buffer reusable once these S complete
                 issued = true;
                 ++sb;
-                if (++sj == nkv) { sj = 0; ++sli; }
+                if (++sj == scnt) { sj = 0; ++sli; scnt = count_of(sli); }
                 if (++ss == kKVStages) { ss = 0; sph ^= 1; }
                 return true;
             };
             if (total > 0) ok = issue_s();
-            int j = 0, li = 0, s = 0;
+            int j = 0, li = 0, s = 0, cnt = count_of(0);
             for (int b = 0; ok && b < total; ++b) {
                 if (b + 1 < total && !issue_s()) {
                     ok = false;
@@ -234,7 +259,7 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
                 for (int k = 0; k < kBKV / 16; ++k) umma_f16_ts(tO, tP + 8 * k, dv + 64 * k, idO, (j | k) != 0);
                 umma_commit(kv_empty + s);
                 umma_commit(o_done + (b & 1));
-                if (++j == nkv) { j = 0; ++li; }
+                if (++j == cnt) { j = 0; ++li; cnt = count_of(li); }
                 if (++s == kKVStages) s = 0;
             }
             if (!ok && issued) {
@@ -247,7 +272,7 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
         const int row = quarter * 32 + lane;
         const uint32_t lane_off = uint32_t(quarter * 32) << 16;
         const float sl2 = a.scale_log2;
-        const bool any_mask = a.key_mask != nullptr;
+        constexpr bool any_mask = MASK;
         const bool ragged = (a.kv_len % kBKV) != 0;
         // m_run is the (log2-domain) max the P values of this row are taken
         // relative to.  It is only raised when a block's max exceeds it by
@@ -258,7 +283,7 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
         bool ok = true;
         int b = 0, li = 0;
         for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++li) {
-            const Item it = item_of(w, n_qt);
+            const Item it = item_of(w, n_qt, splits, nkv);
             const int ob = li & 1;
             const uint32_t tO = tmem + kTmemO + ob * kD;
             const float* mask_row = nullptr;
@@ -270,7 +295,33 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
                 mask_row = a.key_mask + int64_t(it.seq) * a.kv_len;
             }
             float m_run = -INFINITY, l_run = 0.f;
-            for (int j = 0; j < nkv; ++j, ++b) {
+            for (int j = it.j0; j < it.j1; ++j, ++b) {
+                // A block with masked keys (a mask was given, or keys past
+                // kv_len) reads its 64 mask entries before waiting for S, so
+                // the loads overlap the wait; -inf marks a key that takes no
+                // part.
+                const bool masked_blk = any_mask || (ragged && j == nkv - 1);
+                float mv[MASK ? kBKV : 1];
+                if constexpr (MASK) {
+                    const int k0 = j * kBKV;
+                    if (any_mask && k0 + kBKV <= a.kv_len && (reinterpret_cast<uintptr_t>(mask_row + k0) & 15) == 0) {
+                        const float4* m4 = reinterpret_cast<const float4*>(mask_row + k0);
+#pragma unroll
+                        for (int c = 0; c < kBKV / 4; ++c) {
+                            const float4 t = __ldg(m4 + c);
+                            mv[4 * c] = t.x;
+                            mv[4 * c + 1] = t.y;
+                            mv[4 * c + 2] = t.z;
+                            mv[4 * c + 3] = t.w;
+                        }
+                    } else {
+#pragma unroll
+                        for (int c = 0; c < kBKV; ++c) {
+                            const int kk = k0 + c;
+                            mv[c] = kk < a.kv_len ? __ldg(mask_row + kk) : -INFINITY;
+                        }
+                    }
+                }
                 if (!mbar_wait(s_full, b & 1, a.status, kErrTimeoutEpilogue, abort_flag)) {
                     ok = false;
                     break;
@@ -284,22 +335,22 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
                 __syncwarp();
                 if (lane == 0) mbar_arrive(s_free);
 
-                // Scores in the log2 domain are r * sc.  A block with masked
-                // keys (a mask was given, or keys past kv_len) is converted in
-                // place first: s*scale*log2e + mask*log2e, or -inf for a key
-                // that takes no part; it then uses sc = 1.
+                // Scores in the log2 domain are r * sc.  A masked block is
+                // converted in place first: s*scale*log2e + mask*log2e, or
+                // -inf for a key that takes no part; it then uses sc = 1.
                 float sc = sl2;
-                if (any_mask || (ragged && j == nkv - 1)) {
+                if constexpr (MASK) {
+#pragma unroll
+                    for (int c = 0; c < kBKV; ++c)
+                        r[c] = __float_as_uint(mv[c] != -INFINITY ? fmaf(__uint_as_float(r[c]), sl2, mv[c] * kLog2e)
+                                                                 : -INFINITY);
+                    sc = 1.0f;
+                } else if (masked_blk) {
+                    // No mask: only the keys past kv_len of the last block drop out.
                     const int k0 = j * kBKV;
 #pragma unroll
-                    for (int c = 0; c < kBKV; ++c) {
-                        const int kk = k0 + c;
-                        bool valid = kk < a.kv_len;
-                        float mv = 0.f;
-                        if (valid && any_mask) mv = __ldg(mask_row + kk);
-                        valid = valid && mv != -INFINITY;
-                        r[c] = __float_as_uint(valid ? fmaf(__uint_as_float(r[c]), sl2, mv * kLog2e) : -INFINITY);
-                    }
+                    for (int c = 0; c < kBKV; ++c)
+                        r[c] = __float_as_uint(k0 + c < a.kv_len ? __uint_as_float(r[c]) * sl2 : -INFINITY);
                     sc = 1.0f;
                 }
 
@@ -341,7 +392,7 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
                     }
                 }
                 // Rescaling O needs the PV of block b-1 (same item) to have completed.
-                if (j > 0 && __any_sync(0xffffffffu, raise)) {
+                if (j > it.j0 && __any_sync(0xffffffffu, raise)) {
                     if (!mbar_wait(o_done + ((b - 1) & 1), ((b - 1) >> 1) & 1, a.status, kErrTimeoutEpilogue,
                                    abort_flag)) {
                         ok = false;
@@ -377,7 +428,16 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
             __syncwarp();
             if (lane == 0) mbar_arrive(o_free + ob);
             const int qi = it.qt * kBQ + row;
-            if (qi < a.q_len) {
+            if (splits > 1 && qi < a.q_len) {
+                // One key range of the row: unnormalised O and (m, l), merged by mha32_combine.
+                const int64_t p = partial_index(it.seq, it.head, it.qt, row, it.split, n_qt, splits);
+                float4* dst = reinterpret_cast<float4*>(a.ws_o + p * kD);
+#pragma unroll
+                for (int c = 0; c < 8; ++c)
+                    dst[c] = make_float4(__uint_as_float(o[4 * c]), __uint_as_float(o[4 * c + 1]),
+                                         __uint_as_float(o[4 * c + 2]), __uint_as_float(o[4 * c + 3]));
+                *reinterpret_cast<float2*>(a.ws_ml + 2 * p) = make_float2(m_run, l_run);
+            } else if (qi < a.q_len) {
                 const float inv = l_run == 0.0f ? 0.0f : 1.0f / l_run;
                 float v[32];
 #pragma unroll
@@ -406,12 +466,76 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
     }
 }
 
+// Merges the key-range partials of each (sequence, head, query row):
+// O = sum_s O_s 2^(m_s - M) / sum_s l_s 2^(m_s - M), M = max_s m_s; a row
+// whose every range saw only masked keys (all m_s = -inf) is 0.  One thread
+// per (sequence, row, head), heads fastest, so a warp writes 4 whole rows.
+__global__ void __launch_bounds__(256) mha32_combine(const MhaArgs a) {
+    const int64_t t = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t total = int64_t(a.batch) * a.q_len * kHeadsE;
+    if (t >= total) return;
+    const int head = int(t % kHeadsE);
+    const int64_t r = t / kHeadsE;
+    const int qi = int(r % a.q_len);
+    const int seq = int(r / a.q_len);
+    const int n_qt = (a.q_len + kBQ - 1) / kBQ;
+    const int splits = a.splits;
+    const int64_t p0 = partial_index(seq, head, qi / kBQ, qi % kBQ, 0, n_qt, splits);
+    float m_max = -INFINITY;
+    for (int s = 0; s < splits; ++s) m_max = fmaxf(m_max, a.ws_ml[2 * (p0 + s)]);
+    float acc[kD];
+#pragma unroll
+    for (int d = 0; d < kD; ++d) acc[d] = 0.0f;
+    float l = 0.0f;
+    if (m_max != -INFINITY) {
+        for (int s = 0; s < splits; ++s) {
+            const float m = a.ws_ml[2 * (p0 + s)];
+            if (m == -INFINITY) continue;
+            const float w = exp2f(m - m_max);
+            l = fmaf(w, a.ws_ml[2 * (p0 + s) + 1], l);
+            const float4* src = reinterpret_cast<const float4*>(a.ws_o + (p0 + s) * kD);
+#pragma unroll
+            for (int c = 0; c < kD / 4; ++c) {
+                const float4 o = src[c];
+                acc[4 * c] = fmaf(w, o.x, acc[4 * c]);
+                acc[4 * c + 1] = fmaf(w, o.y, acc[4 * c + 1]);
+                acc[4 * c + 2] = fmaf(w, o.z, acc[4 * c + 2]);
+                acc[4 * c + 3] = fmaf(w, o.w, acc[4 * c + 3]);
+            }
+        }
+    }
+    const float inv = l == 0.0f ? 0.0f : 1.0f / l;
+    const int64_t off = (int64_t(seq) * a.q_len + qi) * kModelE + head * kD;
+    if (a.out_f16) {
+        uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.out) + off);
+        for (int c = 0; c < 4; ++c) {
+            uint32_t w4[4];
+            for (int i = 0; i < 4; ++i) {
+                const float x0 = acc[8 * c + 2 * i] * inv, x1 = acc[8 * c + 2 * i + 1] * inv;
+                w4[i] = a.bf16 ? pack_bf162(x0, x1) : pack_half2(x0, x1);
+            }
+            dst[c] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+        }
+    } else {
+        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + off);
+#pragma unroll
+        for (int c = 0; c < kD / 4; ++c)
+            dst[c] = make_float4(acc[4 * c] * inv, acc[4 * c + 1] * inv, acc[4 * c + 2] * inv, acc[4 * c + 3] * inv);
+    }
+}
+
 }  // namespace
 
 cudaError_t mha32_prepare() {
-    cudaError_t e = cudaFuncSetAttribute(mha32_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kMhaSmem));
-    if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(mha32_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kMhaSmem));
+    const void* fns[4] = {reinterpret_cast<const void*>(mha32_kernel<0, false>),
+                          reinterpret_cast<const void*>(mha32_kernel<1, false>),
+                          reinterpret_cast<const void*>(mha32_kernel<0, true>),
+                          reinterpret_cast<const void*>(mha32_kernel<1, true>)};
+    for (const void* f : fns) {
+        const cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kMhaSmem));
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
 }
 
 cudaError_t launch_mha32(const MhaArgs& a, cudaStream_t stream) {
@@ -437,13 +561,51 @@ cudaError_t launch_mha32(const MhaArgs& a, cudaStream_t stream) {
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const int64_t items64 = int64_t((a.q_len + kBQ - 1) / kBQ) * kHeadsE * a.batch;
     if (items64 > (int64_t(1) << 30)) return cudaErrorInvalidValue;
-    const int n_items = int(items64);
-    const int grid = n_items < sms * kCtasPerSm ? n_items : sms * kCtasPerSm;
-    if (a.bf16)
-        mha32_kernel<1><<<grid, 192, kMhaSmem, stream>>>(tq, tk, tv, a);
+    // Too few query tiles to fill the GPU (two CTAs per SM) and enough keys to
+    // pay for the merge (16 blocks or more): split each tile's key blocks into
+    // ranges of at least two blocks, about one wave in all.
+    const int slots = sms * kCtasPerSm;
+    const int nkv = (a.kv_len + kBKV - 1) / kBKV;
+    int splits = 1;
+    if (items64 * 2 <= slots && nkv >= 16) {
+        const int want = int((slots + items64 - 1) / items64);
+        splits = want < nkv / 2 ? want : nkv / 2;
+    }
+    MhaArgs b = a;
+    b.splits = splits;
+    b.ws_o = b.ws_ml = nullptr;
+    void* ws = nullptr;
+    if (splits > 1) {
+        // Stream-ordered scratch for the partials, freed after the merge.
+        const size_t rows = size_t(items64) * kBQ * splits;
+        const size_t bytes_o = rows * kD * sizeof(float);
+        cudaError_t e = cudaMallocAsync(&ws, bytes_o + rows * 2 * sizeof(float), stream);
+        if (e != cudaSuccess) return e;
+        b.ws_o = static_cast<float*>(ws);
+        b.ws_ml = reinterpret_cast<float*>(static_cast<char*>(ws) + bytes_o);
+    }
+    const int n_items = int(items64) * splits;
+    const int grid = n_items < slots ? n_items : slots;
+    const bool masked = b.key_mask != nullptr;
+    if (b.bf16 && masked)
+        mha32_kernel<1, true><<<grid, 192, kMhaSmem, stream>>>(tq, tk, tv, b);
+    else if (b.bf16)
+        mha32_kernel<1, false><<<grid, 192, kMhaSmem, stream>>>(tq, tk, tv, b);
+    else if (masked)
+        mha32_kernel<0, true><<<grid, 192, kMhaSmem, stream>>>(tq, tk, tv, b);
     else
-        mha32_kernel<0><<<grid, 192, kMhaSmem, stream>>>(tq, tk, tv, a);
-    return cudaGetLastError();
+        mha32_kernel<0, false><<<grid, 192, kMhaSmem, stream>>>(tq, tk, tv, b);
+    cudaError_t e = cudaGetLastError();
+    if (splits > 1) {
+        if (e == cudaSuccess) {
+            const int64_t threads = int64_t(a.batch) * a.q_len * kHeadsE;
+            mha32_combine<<<unsigned((threads + 255) / 256), 256, 0, stream>>>(b);
+            e = cudaGetLastError();
+        }
+        const cudaError_t f = cudaFreeAsync(ws, stream);
+        if (e == cudaSuccess) e = f;
+    }
+    return e;
 }
 
 }  // namespace s3t

@@ -188,6 +188,41 @@ def test_mha_decoder_image_cross_attention_full(s3t, torch_cuda, oracle):
     assert cosine(got, ref) > 0.9999
 
 
+def test_mha_split_key_ranges(s3t, torch_cuda, oracle):
+    # Few query tiles against many keys: the kernel splits each tile's keys
+    # into ranges and merges the partials.  Sequence 0 has a long run of masked
+    # keys (whole ranges see nothing but -inf) and scattered masked keys;
+    # sequence 1 has every key masked and must come out 0.
+    import torch
+    B, nq, nk = 2, 100, 2000
+    rng = np.random.default_rng(77)
+    qs, ks, vs = zip(*(_inputs(90 + b, nq, nk) for b in range(B)))
+    mask = np.zeros((B, nk), np.float32)
+    mask[0, 256:1280] = -np.inf
+    mask[0, rng.random(nk) < 0.1] = -np.inf
+    mask[0, 7] = 0.5
+    mask[1, :] = -np.inf
+    dq, dk, dv = (torch.from_numpy(np.stack(a)).half().cuda().reshape(B, -1, 256) for a in (qs, ks, vs))
+    dm = torch.from_numpy(mask).cuda()
+    for flags, odt in ((0, torch.float32), (s3t.MHA_OUT_F16, torch.float16)):
+        out = torch.full((B, nq, 256), float("nan"), dtype=odt, device="cuda")
+        s3t.mha_d32(0, dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), B, nq, nk, dm.data_ptr(), out.data_ptr(), flags)
+        torch.cuda.synchronize()
+        assert s3t.lib().s3t_device_status(0) == 0
+        got = out.float().cpu().numpy().reshape(B, nq, 8, 32)
+        ref = oracle.attention_masked(qs[0], ks[0], vs[0], SCALE, mask[0])
+        assert rel_l2(got[0], ref) < 2e-3
+        assert cosine(got[0], ref) > 0.9999
+        assert np.all(got[1] == 0.0)
+    # The same rows without a mask, against the oracle too.
+    out = torch.full((B, nq, 256), float("nan"), device="cuda")
+    s3t.mha_d32(0, dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), B, nq, nk, None, out.data_ptr())
+    torch.cuda.synchronize()
+    got = out.cpu().numpy().reshape(B, nq, 8, 32)
+    for b in range(B):
+        assert rel_l2(got[b], oracle.attention_masked(qs[b], ks[b], vs[b], SCALE, None)) < 2e-3
+
+
 def test_mha_rejects_bad_arguments(s3t, torch_cuda):
     import torch
     x = torch.zeros((64, 256), dtype=torch.float16, device="cuda")
