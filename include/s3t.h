@@ -53,6 +53,14 @@ int s3t_set_weight(s3t_ctx *ctx, const char *name, int ggml_type, const int64_t 
  * "<gguf_path>.tensor_map.json" if that file exists. */
 int s3t_load_gguf(s3t_ctx *ctx, const char *gguf_path, const char *tensor_map_path);
 
+/* Check a GGUF file as s3t_load_gguf reads it, without a GPU: header,
+ * metadata, tensor records and every trunk tensor's type and byte range
+ * against the file's length.  Outputs (may be NULL): the number of trunk
+ * tensors and of transformer blocks found.  A truncated or corrupt file
+ * returns -1 with a message, like GgufModel::load returning false
+ * (src/gguf_model.cpp:83-94). */
+int s3t_gguf_inspect(const char *gguf_path, const char *tensor_map_path, int *n_trunk_tensors, int *n_layers);
+
 /* Validate shapes/types of the staged tensors, upload them and convert them
  * to the GEMM operand format (Q8_0 / F32 -> fp16 on the device, patch-embed
  * repacked).  Must be called once before the first run. */
@@ -74,6 +82,16 @@ int s3t_trunk_run(s3t_ctx *ctx, const float *images_nchw, int batch, float *out_
  * tools/export_vision_trunk_reference.py (.stem/.ln_pre/.layer_NN). */
 int s3t_trunk_run_layers(s3t_ctx *ctx, const float *images_nchw, int batch, int n_layers, float *out_nchw, int flags,
                          void *stream);
+
+/* One block of the trunk from a given residual: x_dev [batch*5184][1024]
+ * fp32 token-major (token y*72 + x of each image, the input of block
+ * `layer`) -> out_dev, the same layout, the block's output residual
+ * (norm1, attention with its window partition, proj + residual, norm2, MLP
+ * + residual: one iteration of the layer loop of src/vision_trunk.cpp:377-459).
+ * Per-block parity entry, the counterpart of the per-layer dumps of the
+ * reference's tools/export_vision_trunk_reference.py.  Device pointers on
+ * the context's GPU; synchronous (returns after the block ran). */
+int s3t_trunk_run_block(s3t_ctx *ctx, int layer, const float *x_dev, int batch, float *out_dev, void *stream);
 
 /* The trunk from decoded 8-bit RGB: rgb [batch][height][width][3] uint8
  * (row-major HWC, what stbi_load returns; all images of a call share one
@@ -105,6 +123,13 @@ int s3t_sync(s3t_ctx *ctx, void *stream);
 /* Dequantize GGUF weight bytes on the device to fp32: F16 and Q8_0
  * (dequantize_row_q8_0, ggml/src/ggml-quants.c:436-450).  Device pointers. */
 int s3t_dequantize(int ggml_type, const void *src_dev, int64_t n, float *dst_dev, void *stream);
+
+/* The fp16 GEMM operand that s3t_finalize_weights makes of a linear weight,
+ * with the same conversion: Q8_0 -> fp16(q * d) (the exact product of
+ * dequantize_row_q8_0, ggml/src/ggml-quants.c:436-450, rounded to nearest
+ * even fp16), F32 -> fp16 (round to nearest even), F16 -> unchanged.
+ * Device pointers; dst16 holds n fp16 values. */
+int s3t_weight_operand(int ggml_type, const void *src_dev, int64_t n, void *dst16_dev, void *stream);
 
 /* y16[M][N] = fp16(act(x16[M][K] * w16[N][K]^T + bias)) — the trunk's GEMM
  * (ggml_mul_mat + bias, src/vision_trunk.cpp:50-62).  act: 0 none, 1 GELU-erf.

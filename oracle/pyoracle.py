@@ -299,6 +299,9 @@ class Reference:
             L.ref_flash_attn_masked.argtypes = [_p, _p, _p, _i64, _i64, _i64, _i64, C.c_float, _p, _p, C.c_int]
         if hasattr(L, "ref_decoder_mha"):
             L.ref_decoder_mha.argtypes = [_p, _p, _p, _i64, _i64, _i64, _i64, C.c_float, _p, _p, _p, C.c_int]
+        if hasattr(L, "ref_trunk_block"):
+            L.ref_trunk_stem.argtypes = [_p, _p, _p]
+            L.ref_trunk_block.argtypes = [_p, C.c_int, _p, _p]
 
     def _check(self, rc):
         if rc != 0:
@@ -310,6 +313,14 @@ class Reference:
         sec = C.c_double()
         self._check(self.lib.ref_trunk_run(str(gguf_path).encode(), _ptr(img), _ptr(out), n_threads, C.byref(sec)))
         return out, sec.value
+
+    def load(self, gguf_path, n_threads=0) -> "RefModel":
+        """The reference's GgufModel for gguf_path (CPU backend), for the
+        per-block entry points."""
+        h = self.lib.ref_model_load(str(gguf_path).encode(), n_threads)
+        if not h:
+            raise RuntimeError(self.lib.ref_last_error().decode())
+        return RefModel(self, h)
 
     def mul_mat(self, wtype, w_raw, N, K, x, n_threads=4):
         x = np.ascontiguousarray(x, np.float32)
@@ -401,3 +412,31 @@ class Reference:
         out = np.empty((5184, 1024), np.float32)
         self._check(self.lib.ref_patch_embed(wtype, _ptr(np.ascontiguousarray(w_raw)), _ptr(img), _ptr(out), n_threads))
         return out
+
+
+class RefModel:
+    """A loaded reference GgufModel: the stem and single blocks of the
+    reference trunk as ggml graphs (ref_trunk_stem / ref_trunk_block)."""
+
+    def __init__(self, ref: Reference, handle):
+        self.ref, self.h = ref, handle
+
+    def stem(self, image) -> np.ndarray:
+        img = np.ascontiguousarray(image, np.float32)
+        out = np.empty((5184, 1024), np.float32)
+        self.ref._check(self.ref.lib.ref_trunk_stem(self.h, _ptr(img), _ptr(out)))
+        return out
+
+    def block(self, layer: int, x) -> np.ndarray:
+        x = np.ascontiguousarray(x, np.float32).reshape(5184, 1024)
+        out = np.empty_like(x)
+        self.ref._check(self.ref.lib.ref_trunk_block(self.h, layer, _ptr(x), _ptr(out)))
+        return out
+
+    def close(self):
+        if self.h:
+            self.ref.lib.ref_model_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()

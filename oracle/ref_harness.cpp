@@ -17,9 +17,11 @@
 #include "sam3/vision_trunk.h"
 
 #include <chrono>
+#include <cmath>
 #include <cstdint>
 #include <cstring>
 #include <exception>
+#include <stdexcept>
 #include <string>
 #include <vector>
 
@@ -292,6 +294,209 @@ int ref_patch_embed(int wtype, const void * w, const float * image, float * out,
     if (compute(c.ctx, r, n_threads)) return -1;
     std::memcpy(out, r->data, (size_t) 5184 * 1024 * 4);
     return 0;
+}
+
+
+// ---------------------------------------------------------------------------
+// The stem and one trunk block, each as its own ggml graph (per-block parity).
+//
+// src/vision_trunk.cpp builds the stem and all 32 blocks into one graph
+// (:362-459) from helpers private to that file, so the harness states the same
+// ggml ops in the same order: layer_norm (:64-74); linear over row chunks of
+// qkv (:50-62, :76-102); gpu_win_part / gpu_win_unpart (:235-282);
+// apply_axial_rope (:145-205); apply_attention (:207-228); gelu_erf and the
+// residual adds (:439-458).  ggml's own CPU kernels do all of the arithmetic.
+// That these graphs compute exactly what VisionTrunk::run computes is pinned
+// by tests/golden/block_pin_<fmt>.npz: VisionTrunk::run on files whose other
+// blocks are exact identities (zero proj/fc2 weights and biases).
+
+}  // extern "C"
+
+namespace {
+
+const std::string kTrunkPrefix = "backbone.vision_backbone.trunk";
+constexpr int64_t kC = 1024, kG = 72, kW = 24, kNh = 16, kHd = 64, kPre = 24;
+
+ggml_tensor * need(const sam3::GgufModel & m, const std::string & name) {
+    ggml_tensor * t = m.find_weight(name);
+    if (!t) throw std::runtime_error("missing tensor: " + name);
+    return t;
+}
+
+ggml_tensor * f32(ggml_context * ctx, ggml_tensor * t) {
+    return t->type == GGML_TYPE_F32 ? t : ggml_cast(ctx, t, GGML_TYPE_F32);
+}
+
+ggml_tensor * norm_affine(ggml_context * ctx, ggml_tensor * x, ggml_tensor * g, ggml_tensor * b) {
+    ggml_tensor * y = ggml_norm(ctx, f32(ctx, x), 1e-5f);
+    y = ggml_mul(ctx, y, ggml_repeat(ctx, f32(ctx, g), y));
+    return ggml_add(ctx, y, ggml_repeat(ctx, f32(ctx, b), y));
+}
+
+ggml_tensor * dense(ggml_context * ctx, ggml_tensor * w, ggml_tensor * b, ggml_tensor * x) {
+    ggml_tensor * y = f32(ctx, ggml_mul_mat(ctx, w, x));
+    return ggml_add(ctx, y, ggml_repeat(ctx, f32(ctx, b), y));
+}
+
+// rows [row0, row0 + n) of a [K, N] weight and of its bias
+ggml_tensor * dense_rows(ggml_context * ctx, ggml_tensor * w, ggml_tensor * b, int64_t row0, int64_t n,
+                         ggml_tensor * x) {
+    ggml_tensor * wv = ggml_view_2d(ctx, w, w->ne[0], n, w->nb[1], size_t(row0) * w->nb[1]);
+    ggml_tensor * bv = ggml_view_1d(ctx, b, n, size_t(row0) * ggml_element_size(b));
+    return dense(ctx, wv, bv, x);
+}
+
+// [C, W, H, 1] -> [C, win, win, nWy * nWx], windows numbered wy + nWy * wx
+ggml_tensor * to_windows(ggml_context * ctx, ggml_tensor * x) {
+    const int64_t nw = kG / kW;
+    ggml_tensor * t = ggml_reshape_4d(ctx, x, kC, kW, nw, kG);
+    t = ggml_cont(ctx, ggml_permute(ctx, t, 0, 1, 3, 2));
+    return ggml_reshape_4d(ctx, t, kC, kW, kW, nw * nw);
+}
+
+ggml_tensor * from_windows(ggml_context * ctx, ggml_tensor * x) {
+    const int64_t nw = kG / kW;
+    ggml_tensor * t = ggml_reshape_4d(ctx, x, kC, kW, kG, nw);
+    t = ggml_cont(ctx, ggml_permute(ctx, t, 0, 1, 3, 2));
+    return ggml_reshape_4d(ctx, t, kC, kG, kG, 1);
+}
+
+ggml_tensor * rope_xy(ggml_context * ctx, ggml_tensor * x, ggml_tensor * px, ggml_tensor * py, float scale) {
+    const int64_t h = x->ne[0] / 2;
+    ggml_tensor * a = ggml_view_4d(ctx, x, h, x->ne[1], x->ne[2], x->ne[3], x->nb[1], x->nb[2], x->nb[3], 0);
+    ggml_tensor * b = ggml_view_4d(ctx, x, h, x->ne[1], x->ne[2], x->ne[3], x->nb[1], x->nb[2], x->nb[3],
+                                   size_t(h) * ggml_element_size(x));
+    a = ggml_rope_ext(ctx, a, px, nullptr, int(h), 0, 32768, 10000.0f, scale, 0.0f, 1.0f, 0.0f, 0.0f);
+    b = ggml_rope_ext(ctx, b, py, nullptr, int(h), 0, 32768, 10000.0f, scale, 0.0f, 1.0f, 0.0f, 0.0f);
+    return ggml_concat(ctx, a, b, 0);
+}
+
+std::vector<int32_t> axis_positions(int64_t grid, bool x_axis) {
+    std::vector<int32_t> p(size_t(grid * grid));
+    for (int64_t i = 0; i < grid * grid; ++i) p[size_t(i)] = int32_t(x_axis ? i % grid : i / grid);
+    return p;
+}
+
+// A no_alloc context for one graph plus the scheduler over the model's backend.
+struct OneGraph {
+    static constexpr size_t kNodes = 8192;
+    std::vector<uint8_t> meta;
+    ggml_context * ctx = nullptr;
+    ggml_backend_sched_t sched = nullptr;
+    ggml_backend_t backend = nullptr;
+    std::vector<std::pair<ggml_tensor *, const void *>> inputs;
+
+    explicit OneGraph(const sam3::GgufModel & m) : backend(m.backend()) {
+        meta.resize(ggml_tensor_overhead() * kNodes + ggml_graph_overhead_custom(kNodes, false));
+        ggml_init_params p{meta.size(), meta.data(), true};
+        ctx = ggml_init(p);
+        sched = ggml_backend_sched_new(&backend, nullptr, 1, kNodes, false, true);
+        if (!ctx || !sched) throw std::runtime_error("graph setup failed");
+    }
+    ~OneGraph() {
+        if (sched) ggml_backend_sched_free(sched);
+        if (ctx) ggml_free(ctx);
+    }
+    ggml_tensor * input(ggml_type t, int64_t n0, int64_t n1, int64_t n2, int64_t n3, const void * data) {
+        ggml_tensor * x = ggml_new_tensor_4d(ctx, t, n0, n1, n2, n3);
+        inputs.emplace_back(x, data);
+        return x;
+    }
+    void run(ggml_tensor * out, float * dst) {
+        ggml_cgraph * gf = ggml_new_graph_custom(ctx, kNodes, false);
+        ggml_build_forward_expand(gf, out);
+        for (auto & in : inputs) ggml_backend_sched_set_tensor_backend(sched, in.first, backend);
+        if (!ggml_backend_sched_alloc_graph(sched, gf)) throw std::runtime_error("graph allocation failed");
+        for (auto & in : inputs) ggml_backend_tensor_set(in.first, in.second, 0, ggml_nbytes(in.first));
+        if (ggml_backend_sched_graph_compute(sched, gf) != GGML_STATUS_SUCCESS)
+            throw std::runtime_error("graph compute failed");
+        ggml_backend_tensor_get(out, dst, 0, ggml_nbytes(out));
+    }
+};
+
+}  // namespace
+
+extern "C" {
+
+// Patch embed + tiled position embedding + ln_pre (src/vision_trunk.cpp:284-291,
+// 111-132, 362-374) of the model behind `handle` (ref_model_load).
+// image [3][1008][1008] f32 -> out [5184][1024] f32, token t = y*72 + x.
+int ref_trunk_stem(void * handle, const float * image, float * out) {
+    try {
+        const auto & m = *static_cast<const sam3::GgufModel *>(handle);
+        ggml_tensor * pe = need(m, kTrunkPrefix + ".pos_embed");
+        if (ggml_nelements(pe) != (kPre * kPre + 1) * kC) throw std::runtime_error("unexpected trunk.pos_embed size");
+        std::vector<float> pos(size_t(ggml_nelements(pe)));
+        ggml_backend_tensor_get(pe, pos.data(), 0, pos.size() * 4);
+        std::vector<float> tiled(size_t(kG * kG * kC));
+        for (int64_t t = 0; t < kG * kG; ++t) {
+            const int64_t src = 1 + (t / kG % kPre) * kPre + (t % kG % kPre);
+            std::memcpy(&tiled[size_t(t * kC)], &pos[size_t(src * kC)], kC * 4);
+        }
+        OneGraph g(m);
+        ggml_tensor * img = g.input(GGML_TYPE_F32, 1008, 1008, 3, 1, image);
+        ggml_tensor * abs_pos = g.input(GGML_TYPE_F32, kC, kG, kG, 1, tiled.data());
+        ggml_tensor * w = need(m, kTrunkPrefix + ".patch_embed.proj.weight");
+        ggml_tensor * cur = ggml_conv_2d(g.ctx, ggml_cont(g.ctx, ggml_permute(g.ctx, w, 2, 0, 1, 3)), img,
+                                         14, 14, 0, 0, 1, 1);
+        cur = ggml_cont(g.ctx, ggml_permute(g.ctx, cur, 1, 2, 0, 3));
+        cur = ggml_add(g.ctx, cur, abs_pos);
+        cur = norm_affine(g.ctx, cur, need(m, kTrunkPrefix + ".ln_pre.weight"), need(m, kTrunkPrefix + ".ln_pre.bias"));
+        g.run(cur, out);
+        return 0;
+    } catch (const std::exception & e) {
+        g_err = e.what();
+        return -1;
+    }
+}
+
+// Block `layer` of the trunk (src/vision_trunk.cpp:377-459) on the model behind
+// `handle`: x [5184][1024] f32 (the block's input residual, token-major) ->
+// out [5184][1024] f32 (its output residual).
+int ref_trunk_block(void * handle, int layer, const float * x, float * out) {
+    try {
+        const auto & m = *static_cast<const sam3::GgufModel *>(handle);
+        const std::string b = kTrunkPrefix + ".blocks." + std::to_string(layer);
+        const bool global = layer == 7 || layer == 15 || layer == 23 || layer == 31;
+        const int64_t side = global ? kG : kW;
+        const std::vector<int32_t> px = axis_positions(side, true), py = axis_positions(side, false);
+        OneGraph g(m);
+        ggml_context * ctx = g.ctx;
+        ggml_tensor * inp = g.input(GGML_TYPE_F32, kC, kG, kG, 1, x);
+        ggml_tensor * pos_x = g.input(GGML_TYPE_I32, side * side, 1, 1, 1, px.data());
+        ggml_tensor * pos_y = g.input(GGML_TYPE_I32, side * side, 1, 1, 1, py.data());
+
+        ggml_tensor * cur = norm_affine(ctx, inp, need(m, b + ".norm1.weight"), need(m, b + ".norm1.bias"));
+        if (!global) cur = to_windows(ctx, cur);
+        const int64_t w = cur->ne[1], h = cur->ne[2], nb = cur->ne[3], tokens = w * h;
+        ggml_tensor * qw = need(m, b + ".attn.qkv.weight");
+        ggml_tensor * qb = need(m, b + ".attn.qkv.bias");
+        ggml_tensor * q = ggml_reshape_4d(ctx, dense_rows(ctx, qw, qb, 0, kC, cur), kHd, kNh, tokens, nb);
+        ggml_tensor * k = ggml_reshape_4d(ctx, dense_rows(ctx, qw, qb, kC, kC, cur), kHd, kNh, tokens, nb);
+        ggml_tensor * v = ggml_reshape_4d(ctx, dense_rows(ctx, qw, qb, 2 * kC, kC, cur), kHd, kNh, tokens, nb);
+        const float scale = global ? float(kW) / float(kG) : 1.0f;
+        q = rope_xy(ctx, q, pos_x, pos_y, scale);
+        k = rope_xy(ctx, k, pos_x, pos_y, scale);
+        ggml_tensor * att = ggml_flash_attn_ext(ctx, ggml_permute(ctx, q, 0, 2, 1, 3), ggml_permute(ctx, k, 0, 2, 1, 3),
+                                                ggml_permute(ctx, v, 0, 2, 1, 3), nullptr, 1.0f / std::sqrt(float(kHd)),
+                                                0.0f, 0.0f);
+        ggml_flash_attn_ext_set_prec(att, GGML_PREC_F32);
+        att = ggml_reshape_2d(ctx, att, att->ne[0] * att->ne[1], att->ne[2] * att->ne[3]);
+        att = ggml_reshape_4d(ctx, att, kC, w, h, nb);
+        att = dense(ctx, need(m, b + ".attn.proj.weight"), need(m, b + ".attn.proj.bias"), att);
+        if (!global) att = from_windows(ctx, att);
+        cur = ggml_add(ctx, inp, att);
+
+        ggml_tensor * ffn = norm_affine(ctx, cur, need(m, b + ".norm2.weight"), need(m, b + ".norm2.bias"));
+        ffn = dense(ctx, need(m, b + ".mlp.fc1.weight"), need(m, b + ".mlp.fc1.bias"), ffn);
+        ffn = ggml_gelu_erf(ctx, ffn);
+        ffn = dense(ctx, need(m, b + ".mlp.fc2.weight"), need(m, b + ".mlp.fc2.bias"), ffn);
+        g.run(ggml_add(ctx, cur, ffn), out);
+        return 0;
+    } catch (const std::exception & e) {
+        g_err = e.what();
+        return -1;
+    }
 }
 
 }  // extern "C"

@@ -53,12 +53,15 @@ def lib() -> C.CDLL:
         L.s3t_destroy.argtypes = [p]
         L.s3t_set_weight.argtypes = [p, C.c_char_p, i, C.POINTER(i64), p, sz]
         L.s3t_load_gguf.argtypes = [p, C.c_char_p, C.c_char_p]
+        L.s3t_gguf_inspect.argtypes = [C.c_char_p, C.c_char_p, C.POINTER(i), C.POINTER(i)]
         L.s3t_finalize_weights.argtypes = [p]
         L.s3t_num_layers.argtypes = [p]
         L.s3t_trunk_run.argtypes = [p, p, i, p, i, p]
         L.s3t_trunk_run_layers.argtypes = [p, p, i, i, p, i, p]
+        L.s3t_trunk_run_block.argtypes = [p, i, p, i, p, p]
         L.s3t_sync.argtypes = [p, p]
         L.s3t_dequantize.argtypes = [i, p, i64, p, p]
+        L.s3t_weight_operand.argtypes = [i, p, i64, p, p]
         L.s3t_gemm_f16.argtypes = [i, p, p, p, i, i, i, i, i, p, p]
         L.s3t_attention.argtypes = [i, p, p, p, i, i, i, i, p, p]
         L.s3t_rope.argtypes = [i, p, i, i, i, i, p]
@@ -186,6 +189,12 @@ class VisionTrunk:
         else:
             check(L.s3t_trunk_run_layers(self.model.ctx, images.ctypes.data, b, n_layers, out.ctypes.data, 0, None))
         return out
+
+    def run_block_device(self, layer: int, x_ptr: int, batch: int, out_ptr: int, stream: int = 0) -> None:
+        """Block `layer` alone on device residuals [batch*5184][1024] fp32
+        (token-major): s3t_trunk_run_block.  Synchronous."""
+        check(lib().s3t_trunk_run_block(self.model.ctx, layer, C.c_void_p(x_ptr), batch, C.c_void_p(out_ptr),
+                                        C.c_void_p(stream) if stream else None))
 
     def run_rgb8(self, rgb: np.ndarray) -> np.ndarray:
         """Decoded 8-bit RGB [h, w, 3] or [B, h, w, 3] uint8 (stbi_load layout,

@@ -245,6 +245,101 @@ void load_aliases(const std::string& path, std::unordered_map<std::string, std::
     }
 }
 
+// A GGUF file mapped read-only, with its trunk tensors under their original
+// names (the converter's hashed names resolved through the sidecar).  Every
+// count, size and offset read from the file is checked against the file's
+// length before it is used, so a truncated or corrupt file is an error, not
+// an out-of-bounds read or a huge allocation.
+struct GgufFile {
+    void* map = MAP_FAILED;
+    size_t size = 0;
+    struct Tensor {
+        uint32_t type;
+        int64_t ne[4];
+        uint64_t offset;   // from the start of the file
+        uint64_t nbytes;
+    };
+    std::vector<std::pair<std::string, Tensor>> trunk;
+    const uint8_t* base() const { return static_cast<const uint8_t*>(map); }
+    ~GgufFile() {
+        if (map != MAP_FAILED) munmap(map, size);
+    }
+};
+
+int open_gguf(const char* path, const char* map_path, GgufFile& f) {
+    const int fd = open(path, O_RDONLY);
+    if (fd < 0) return fail(std::string("cannot open ") + path);
+    struct stat stt;
+    if (fstat(fd, &stt) != 0) {
+        close(fd);
+        return fail(std::string("cannot stat ") + path);
+    }
+    f.size = size_t(stt.st_size);
+    if (f.size < 24) {
+        close(fd);
+        return fail(std::string("not a GGUF file (too short): ") + path);
+    }
+    f.map = mmap(nullptr, f.size, PROT_READ, MAP_PRIVATE, fd, 0);
+    close(fd);
+    if (f.map == MAP_FAILED) return fail(std::string("mmap failed for ") + path);
+    const uint8_t* base = f.base();
+    Reader r{base, base + f.size};
+    if (r.get<uint32_t>() != 0x46554747u) return fail("not a GGUF file");   // "GGUF"
+    const uint32_t version = r.get<uint32_t>();
+    if (version < 2 || version > 3) return fail("unsupported GGUF version " + std::to_string(version));
+    const uint64_t n_tensors = r.get<uint64_t>();
+    const uint64_t n_kv = r.get<uint64_t>();
+    const uint64_t rest = uint64_t(r.end - r.p);
+    // A tensor record takes at least 24 bytes (name length, dims, type,
+    // offset) and a key/value pair at least 13 (key length, type, a value).
+    if (n_tensors > rest / 24) return fail("corrupt GGUF header: tensor count " + std::to_string(n_tensors));
+    if (n_kv > rest / 13) return fail("corrupt GGUF header: metadata count " + std::to_string(n_kv));
+    uint32_t alignment = 32;   // gguf.h GGUF_DEFAULT_ALIGNMENT
+    for (uint64_t i = 0; i < n_kv && r.ok; ++i) {
+        const std::string key = r.str();
+        const uint32_t vt = r.get<uint32_t>();
+        uint32_t u = 0;
+        if (!skip_value(r, vt, key == "general.alignment" ? &u : nullptr)) r.ok = false;
+        if (key == "general.alignment" && u) alignment = u;
+    }
+    if (!r.ok) return fail("truncated GGUF metadata");
+    if (alignment & (alignment - 1)) return fail("corrupt GGUF header: alignment " + std::to_string(alignment));
+    std::vector<GgufTensor> ts(n_tensors);
+    for (uint64_t i = 0; i < n_tensors && r.ok; ++i) {
+        ts[i].name = r.str();
+        const uint32_t nd = r.get<uint32_t>();
+        if (nd > 4) return fail("corrupt GGUF tensor record: " + std::to_string(nd) + " dimensions");
+        for (uint32_t d = 0; d < nd; ++d) ts[i].ne[d] = int64_t(r.get<uint64_t>());
+        ts[i].type = r.get<uint32_t>();
+        ts[i].offset = r.get<uint64_t>();
+    }
+    if (!r.ok) return fail("truncated GGUF header");
+    const uint64_t hdr = uint64_t(r.p - base);
+    const uint64_t data = (hdr + alignment - 1) / alignment * alignment;
+    std::unordered_map<std::string, std::string> o2s;
+    load_aliases(map_path ? std::string(map_path) : std::string(path) + ".tensor_map.json", o2s);
+    std::unordered_map<std::string, std::string> s2o;   // hashed name -> original
+    for (const auto& kv : o2s)
+        if (kv.first != kv.second) s2o[kv.second] = kv.first;
+    for (const auto& t : ts) {
+        auto al = s2o.find(t.name);
+        const std::string& orig = al != s2o.end() ? al->second : t.name;
+        if (orig.rfind(kPrefix, 0) != 0) continue;
+        int64_t n = 1;
+        for (int d = 0; d < 4; ++d) {
+            if (t.ne[d] <= 0 || t.ne[d] > (int64_t(1) << 40) / n) return fail("corrupt GGUF shape for " + orig);
+            n *= t.ne[d];
+        }
+        const int64_t nb = type_nbytes(int(t.type), n);
+        if (nb < 0) return fail("unsupported tensor type in " + orig);
+        if (data > f.size || t.offset > f.size - data || uint64_t(nb) > f.size - data - t.offset)
+            return fail("tensor data out of file bounds: " + orig);
+        GgufFile::Tensor tt{t.type, {t.ne[0], t.ne[1], t.ne[2], t.ne[3]}, data + t.offset, uint64_t(nb)};
+        f.trunk.emplace_back(orig, tt);
+    }
+    return 0;
+}
+
 }  // namespace
 
 // ---------------------------------------------------------------- context ---
@@ -294,7 +389,16 @@ struct s3t_ctx {
     uint8_t* rgb = nullptr;   // device copy of host uint8 images (s3t_trunk_run_rgb8)
     size_t rgb_cap = 0;
 
-    std::map<GraphKey, cudaGraphExec_t> graphs;
+    // Captured trunk graphs by (batch, layers, input, output), at most
+    // kMaxGraphs of them; the least recently launched one is dropped beyond
+    // that (a caller whose allocator hands out fresh buffers on every call
+    // would otherwise capture a new graph per call and never free one).
+    struct CachedGraph {
+        cudaGraphExec_t exec;
+        uint64_t last_use;
+    };
+    std::map<GraphKey, CachedGraph> graphs;
+    uint64_t graph_clock = 0;
     cudaStream_t copy_in = nullptr, copy_out = nullptr;   // host-buffer pipelining
     std::vector<cudaEvent_t> events;
     // Set only during s3t_trunk_profile: an event is recorded after every launch.
@@ -313,8 +417,10 @@ int dev_alloc(std::vector<void*>& list, T** p, size_t bytes) {
     return 0;
 }
 
+constexpr size_t kMaxGraphs = 8;
+
 void free_graphs(s3t_ctx* c) {
-    for (auto& kv : c->graphs) cudaGraphExecDestroy(kv.second);
+    for (auto& kv : c->graphs) cudaGraphExecDestroy(kv.second.exec);
     c->graphs.clear();
 }
 
@@ -360,6 +466,80 @@ int mark(s3t_ctx* c, cudaStream_t st, int kind) {
         if (mark(c, st, (kind))) return -1;     \
     } while (0)
 
+// Enqueue block l on the residual c->x, whose norm1 output is already in
+// c->a16: QKV GEMM + RoPE + window scatter, attention, proj GEMM + residual,
+// LayerNorm, fc1 GEMM + GELU, fc2 GEMM + residual (src/vision_trunk.cpp:377-459).
+// out_nchw: also write the block's output as NCHW (last block), or null.
+int enqueue_block(s3t_ctx* c, int l, int batch, float* out_nchw, cudaStream_t st) {
+    const int M = batch * kTokens;
+    const int sms = c->dev->num_sms;
+    int* status = c->dev->status;
+    const int64_t qkv_stride = int64_t(M) * kDim;
+    const LayerW& w = c->layers[l];
+    const bool glob = is_global_attention_block(l);
+
+    GemmArgs q{};
+    q.M = M; q.N = 3 * kDim; q.K = kDim;
+    q.bias = w.qkv_b;
+    q.qkv = c->qkv;
+    q.qkv_stride = qkv_stride;
+    q.windowed = glob ? 0 : 1;
+    q.rope_local = c->dev->rope_local;
+    q.rope_global = c->dev->rope_global;
+    q.rope_local_t = c->dev->rope_local_t;
+    q.rope_global_t = c->dev->rope_global_t;
+    q.status = status;
+    S3T_CUDA(launch_gemm(c->a16, w.qkv, q, kEpiQkv, sms, st));
+    S3T_MARK(kProfQkv);
+
+    AttnArgs at{};
+    at.q = c->qkv;
+    at.k = c->qkv + qkv_stride;
+    at.v = c->qkv + 2 * qkv_stride;
+    at.groups = glob ? batch : batch * 9;
+    at.L = glob ? kTokens : kWindow * kWindow;
+    at.windowed = glob ? 0 : 1;
+    at.scale_log2 = 0.125f * 1.4426950408889634f;
+    at.bf16 = 0;
+    at.q8 = w.proj_t == S3T_TYPE_Q8_0;
+    at.out = c->attn;
+    at.status = status;
+    S3T_CUDA(launch_attention(at, st));
+    S3T_MARK(glob ? kProfAttnGlob : kProfAttnWin);
+
+    GemmArgs p{};
+    p.M = M; p.N = kDim; p.K = kDim;
+    p.bias = w.proj_b;
+    p.resid = c->x;
+    p.status = status;
+    S3T_CUDA(launch_gemm(c->attn, w.proj, p, kEpiResid, sms, st));
+    S3T_MARK(kProfProj);
+
+    S3T_CUDA(launch_layernorm(c->x, M, w.n2w, w.n2b, c->a16, w.fc1_t == S3T_TYPE_Q8_0, st));
+    S3T_MARK(kProfNorm);
+
+    GemmArgs f1{};
+    f1.M = M; f1.N = kMlp; f1.K = kDim;
+    f1.bias = w.fc1_b;
+    f1.out16 = c->h;
+    f1.gelu = 1;
+    f1.q8 = w.fc2_t == S3T_TYPE_Q8_0;
+    f1.status = status;
+    S3T_CUDA(launch_gemm(c->a16, w.fc1, f1, kEpiF16, sms, st));
+    S3T_MARK(kProfFc1);
+
+    GemmArgs f2{};
+    f2.M = M; f2.N = kDim; f2.K = kMlp;
+    f2.bias = w.fc2_b;
+    f2.resid = c->x;
+    f2.out_nchw = out_nchw;
+    f2.status = status;
+    S3T_CUDA(launch_gemm(c->h, w.fc2, f2, kEpiResid, sms, st));
+    S3T_MARK(kProfFc2);
+
+    return 0;
+}
+
 int enqueue_trunk(s3t_ctx* c, const float* images, int batch, int n_layers, float* out, cudaStream_t st) {
     const int M = batch * kTokens;
     const int sms = c->dev->num_sms;
@@ -380,70 +560,8 @@ int enqueue_trunk(s3t_ctx* c, const float* images, int batch, int n_layers, floa
                                    c->layers[0].qkv_t == S3T_TYPE_Q8_0, st));
     S3T_MARK(kProfStem);
 
-    const int64_t qkv_stride = int64_t(M) * kDim;
     for (int l = 0; l < n_layers; ++l) {
-        const LayerW& w = c->layers[l];
-        const bool glob = is_global_attention_block(l);
-
-        GemmArgs q{};
-        q.M = M; q.N = 3 * kDim; q.K = kDim;
-        q.bias = w.qkv_b;
-        q.qkv = c->qkv;
-        q.qkv_stride = qkv_stride;
-        q.windowed = glob ? 0 : 1;
-        q.rope_local = c->dev->rope_local;
-        q.rope_global = c->dev->rope_global;
-        q.rope_local_t = c->dev->rope_local_t;
-        q.rope_global_t = c->dev->rope_global_t;
-        q.status = status;
-        S3T_CUDA(launch_gemm(c->a16, w.qkv, q, kEpiQkv, sms, st));
-        S3T_MARK(kProfQkv);
-
-        AttnArgs at{};
-        at.q = c->qkv;
-        at.k = c->qkv + qkv_stride;
-        at.v = c->qkv + 2 * qkv_stride;
-        at.groups = glob ? batch : batch * 9;
-        at.L = glob ? kTokens : kWindow * kWindow;
-        at.windowed = glob ? 0 : 1;
-        at.scale_log2 = 0.125f * 1.4426950408889634f;
-        at.bf16 = 0;
-        at.q8 = w.proj_t == S3T_TYPE_Q8_0;
-        at.out = c->attn;
-        at.status = status;
-        S3T_CUDA(launch_attention(at, st));
-        S3T_MARK(glob ? kProfAttnGlob : kProfAttnWin);
-
-        GemmArgs p{};
-        p.M = M; p.N = kDim; p.K = kDim;
-        p.bias = w.proj_b;
-        p.resid = c->x;
-        p.status = status;
-        S3T_CUDA(launch_gemm(c->attn, w.proj, p, kEpiResid, sms, st));
-        S3T_MARK(kProfProj);
-
-        S3T_CUDA(launch_layernorm(c->x, M, w.n2w, w.n2b, c->a16, w.fc1_t == S3T_TYPE_Q8_0, st));
-        S3T_MARK(kProfNorm);
-
-        GemmArgs f1{};
-        f1.M = M; f1.N = kMlp; f1.K = kDim;
-        f1.bias = w.fc1_b;
-        f1.out16 = c->h;
-        f1.gelu = 1;
-        f1.q8 = w.fc2_t == S3T_TYPE_Q8_0;
-        f1.status = status;
-        S3T_CUDA(launch_gemm(c->a16, w.fc1, f1, kEpiF16, sms, st));
-        S3T_MARK(kProfFc1);
-
-        GemmArgs f2{};
-        f2.M = M; f2.N = kDim; f2.K = kMlp;
-        f2.bias = w.fc2_b;
-        f2.resid = c->x;
-        f2.out_nchw = (l == n_layers - 1) ? out : nullptr;
-        f2.status = status;
-        S3T_CUDA(launch_gemm(c->h, w.fc2, f2, kEpiResid, sms, st));
-        S3T_MARK(kProfFc2);
-
+        if (enqueue_block(c, l, batch, (l == n_layers - 1) ? out : nullptr, st)) return -1;
         if (l + 1 < n_layers) {
             const LayerW& nx = c->layers[l + 1];
             S3T_CUDA(launch_layernorm(c->x, M, nx.n1w, nx.n1b, c->a16, nx.qkv_t == S3T_TYPE_Q8_0, st));
@@ -491,6 +609,14 @@ int check_status(s3t_ctx* c, cudaStream_t st) {
 int trunk_graph(s3t_ctx* c, const float* din, int batch, int n_layers, float* dout, cudaGraphExec_t* out) {
     const GraphKey key{batch, n_layers, din, dout};
     auto it = c->graphs.find(key);
+    if (it == c->graphs.end() && c->graphs.size() >= kMaxGraphs) {
+        auto lru = c->graphs.begin();
+        for (auto g = c->graphs.begin(); g != c->graphs.end(); ++g)
+            if (g->second.last_use < lru->second.last_use) lru = g;
+        S3T_CUDA(cudaDeviceSynchronize());   // the evicted graph may still be running
+        S3T_CUDA(cudaGraphExecDestroy(lru->second.exec));
+        c->graphs.erase(lru);
+    }
     if (it == c->graphs.end()) {
         cudaStream_t cap;
         S3T_CUDA(cudaStreamCreateWithFlags(&cap, cudaStreamNonBlocking));
@@ -508,9 +634,10 @@ int trunk_graph(s3t_ctx* c, const float* din, int batch, int n_layers, float* do
         const cudaError_t ei = cudaGraphInstantiate(&exec, graph, 0);
         cudaGraphDestroy(graph);
         S3T_CUDA(ei);
-        it = c->graphs.emplace(key, exec).first;
+        it = c->graphs.emplace(key, s3t_ctx::CachedGraph{exec, 0}).first;
     }
-    *out = it->second;
+    it->second.last_use = ++c->graph_clock;
+    *out = it->second.exec;
     return 0;
 }
 
@@ -629,461 +756,531 @@ bool s3t::ctx_stem_view(const s3t_ctx* c, StemView* out) {
     return true;
 }
 
+// Nothing may throw across the C ABI (std::bad_alloc from a host buffer, a
+// std::length_error from a container): every entry point's body runs inside
+// a try block whose handlers turn an exception into the -1 / last-error
+// convention (NULL for s3t_create; s3t_destroy swallows it).
+#define S3T_CATCH_INT                                                              \
+    catch (const std::bad_alloc&) {                                                \
+        return fail("out of host memory");                                         \
+    }                                                                              \
+    catch (const std::exception& e) {                                              \
+        return fail(std::string("internal error: ") + e.what());                   \
+    }                                                                              \
+    catch (...) {                                                                  \
+        return fail("internal error");                                             \
+    }
+#define S3T_CATCH_PTR                                                              \
+    catch (const std::exception& e) {                                              \
+        fail(std::string("internal error: ") + e.what());                          \
+        return nullptr;                                                            \
+    }                                                                              \
+    catch (...) {                                                                  \
+        fail("internal error");                                                    \
+        return nullptr;                                                            \
+    }
+#define S3T_CATCH_VOID \
+    catch (...) {      \
+    }
+
 extern "C" {
 
 const char* s3t_last_error(void) { return g_last_error.c_str(); }
 
 s3t_ctx* s3t_create(int device) {
-    int n = 0;
-    if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) {
-        fail("no CUDA device " + std::to_string(device));
-        return nullptr;
-    }
-    DeviceState* ds = nullptr;
-    if (device_state(device, &ds)) return nullptr;
-    s3t_ctx* c = new s3t_ctx();
-    c->device = device;
-    c->dev = ds;
-    if (cudaSetDevice(device) != cudaSuccess || cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
-        fail("stream creation failed");
-        delete c;
-        return nullptr;
-    }
-    return c;
+    try {
+        int n = 0;
+        if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) {
+            fail("no CUDA device " + std::to_string(device));
+            return nullptr;
+        }
+        DeviceState* ds = nullptr;
+        if (device_state(device, &ds)) return nullptr;
+        s3t_ctx* c = new s3t_ctx();
+        c->device = device;
+        c->dev = ds;
+        if (cudaSetDevice(device) != cudaSuccess || cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
+            fail("stream creation failed");
+            delete c;
+            return nullptr;
+        }
+        return c;
+    } S3T_CATCH_PTR
 }
 
 void s3t_destroy(s3t_ctx* c) {
-    if (!c) return;
-    cudaSetDevice(c->device);
-    cudaStreamSynchronize(c->stream);
-    free_workspace(c);
-    for (auto& kv : c->staged)
-        if (kv.second.dev) cudaFree(kv.second.dev);
-    for (void* p : c->allocs) cudaFree(p);
-    if (c->rgb) cudaFree(c->rgb);
-    for (cudaEvent_t e : c->events) cudaEventDestroy(e);
-    if (c->copy_in) cudaStreamDestroy(c->copy_in);
-    if (c->copy_out) cudaStreamDestroy(c->copy_out);
-    cudaStreamDestroy(c->stream);
-    delete c;
+    try {
+        if (!c) return;
+        cudaSetDevice(c->device);
+        cudaStreamSynchronize(c->stream);
+        free_workspace(c);
+        for (auto& kv : c->staged)
+            if (kv.second.dev) cudaFree(kv.second.dev);
+        for (void* p : c->allocs) cudaFree(p);
+        if (c->rgb) cudaFree(c->rgb);
+        for (cudaEvent_t e : c->events) cudaEventDestroy(e);
+        if (c->copy_in) cudaStreamDestroy(c->copy_in);
+        if (c->copy_out) cudaStreamDestroy(c->copy_out);
+        cudaStreamDestroy(c->stream);
+        delete c;
+    } S3T_CATCH_VOID
 }
 
 int s3t_set_weight(s3t_ctx* c, const char* name, int type, const int64_t ne[4], const void* bytes, size_t nbytes) {
-    if (!c || !name || !ne || !bytes) return fail("null argument to s3t_set_weight");
-    if (c->finalized) return fail("weights already finalized");
-    int64_t n = 1;
-    for (int i = 0; i < 4; ++i) {
-        if (ne[i] <= 0) return fail(std::string("bad shape for ") + name);
-        n *= ne[i];
-    }
-    const int64_t need = type_nbytes(type, n);
-    if (need < 0) return fail(std::string("unsupported ggml type ") + std::to_string(type) + " for " + name);
-    if (int64_t(nbytes) != need) return fail(std::string("size mismatch for ") + name);
-    Staged s;
-    s.type = type;
-    for (int i = 0; i < 4; ++i) s.ne[i] = ne[i];
-    s.nbytes = nbytes;
-    const std::string nm(name);
-    const bool linear = nm.find(".weight") != std::string::npos &&
-                        (nm.find(".attn.") != std::string::npos || nm.find(".mlp.") != std::string::npos);
-    if (cudaSetDevice(c->device) != cudaSuccess) return fail("cudaSetDevice failed");
-    if (linear) {
-        if (cudaMalloc(&s.dev, nbytes) != cudaSuccess) return fail("cudaMalloc failed for " + nm);
-        cudaError_t e = cudaMemcpy(s.dev, bytes, nbytes, cudaMemcpyHostToDevice);
-        if (e != cudaSuccess) {
-            cudaFree(s.dev);
-            return fail(std::string("upload failed: ") + cudaGetErrorString(e));
+    try {
+        if (!c || !name || !ne || !bytes) return fail("null argument to s3t_set_weight");
+        if (c->finalized) return fail("weights already finalized");
+        int64_t n = 1;
+        for (int i = 0; i < 4; ++i) {
+            if (ne[i] <= 0) return fail(std::string("bad shape for ") + name);
+            n *= ne[i];
         }
-    } else {
-        s.host.assign(static_cast<const uint8_t*>(bytes), static_cast<const uint8_t*>(bytes) + nbytes);
-    }
-    auto it = c->staged.find(nm);
-    if (it != c->staged.end() && it->second.dev) cudaFree(it->second.dev);
-    c->staged[nm] = std::move(s);
-    return 0;
+        const int64_t need = type_nbytes(type, n);
+        if (need < 0) return fail(std::string("unsupported ggml type ") + std::to_string(type) + " for " + name);
+        if (int64_t(nbytes) != need) return fail(std::string("size mismatch for ") + name);
+        Staged s;
+        s.type = type;
+        for (int i = 0; i < 4; ++i) s.ne[i] = ne[i];
+        s.nbytes = nbytes;
+        const std::string nm(name);
+        const bool linear = nm.find(".weight") != std::string::npos &&
+                            (nm.find(".attn.") != std::string::npos || nm.find(".mlp.") != std::string::npos);
+        if (cudaSetDevice(c->device) != cudaSuccess) return fail("cudaSetDevice failed");
+        if (linear) {
+            if (cudaMalloc(&s.dev, nbytes) != cudaSuccess) return fail("cudaMalloc failed for " + nm);
+            cudaError_t e = cudaMemcpy(s.dev, bytes, nbytes, cudaMemcpyHostToDevice);
+            if (e != cudaSuccess) {
+                cudaFree(s.dev);
+                return fail(std::string("upload failed: ") + cudaGetErrorString(e));
+            }
+        } else {
+            s.host.assign(static_cast<const uint8_t*>(bytes), static_cast<const uint8_t*>(bytes) + nbytes);
+        }
+        auto it = c->staged.find(nm);
+        if (it != c->staged.end() && it->second.dev) cudaFree(it->second.dev);
+        c->staged[nm] = std::move(s);
+        return 0;
+    } S3T_CATCH_INT
 }
 
 int s3t_load_gguf(s3t_ctx* c, const char* path, const char* map_path) {
-    if (!c || !path) return fail("null argument to s3t_load_gguf");
-    const int fd = open(path, O_RDONLY);
-    if (fd < 0) return fail(std::string("cannot open ") + path);
-    struct stat stt;
-    fstat(fd, &stt);
-    const size_t size = size_t(stt.st_size);
-    void* map = mmap(nullptr, size, PROT_READ, MAP_PRIVATE, fd, 0);
-    close(fd);
-    if (map == MAP_FAILED) return fail(std::string("mmap failed for ") + path);
-    const uint8_t* base = static_cast<const uint8_t*>(map);
-    Reader r{base, base + size};
-    int rc = 0;
-    do {
-        if (r.get<uint32_t>() != 0x46554747u) { rc = fail("not a GGUF file"); break; }   // "GGUF"
-        const uint32_t version = r.get<uint32_t>();
-        if (version < 2) { rc = fail("unsupported GGUF version"); break; }
-        const uint64_t n_tensors = r.get<uint64_t>();
-        const uint64_t n_kv = r.get<uint64_t>();
-        uint32_t alignment = 32;   // gguf.h GGUF_DEFAULT_ALIGNMENT
-        for (uint64_t i = 0; i < n_kv && r.ok; ++i) {
-            const std::string key = r.str();
-            const uint32_t vt = r.get<uint32_t>();
-            uint32_t u = 0;
-            if (!skip_value(r, vt, key == "general.alignment" ? &u : nullptr)) { r.ok = false; break; }
-            if (key == "general.alignment" && u) alignment = u;
+    try {
+        if (!c || !path) return fail("null argument to s3t_load_gguf");
+        GgufFile f;
+        if (open_gguf(path, map_path, f)) return -1;
+        for (const auto& t : f.trunk)
+            if (s3t_set_weight(c, t.first.c_str(), int(t.second.type), t.second.ne, f.base() + t.second.offset,
+                               size_t(t.second.nbytes)))
+                return -1;
+        return 0;
+    } S3T_CATCH_INT
+}
+
+int s3t_gguf_inspect(const char* path, const char* map_path, int* n_trunk_tensors, int* n_layers) {
+    try {
+        if (!path) return fail("null argument to s3t_gguf_inspect");
+        GgufFile f;
+        if (open_gguf(path, map_path, f)) return -1;
+        int layers = 0;
+        const std::string P(kPrefix);
+        for (bool found = true; found && layers < kLayers;) {
+            found = false;
+            const std::string q = P + ".blocks." + std::to_string(layers) + ".attn.qkv.weight";
+            for (const auto& t : f.trunk) found = found || t.first == q;
+            if (found) ++layers;
         }
-        std::vector<GgufTensor> ts(n_tensors);
-        for (uint64_t i = 0; i < n_tensors && r.ok; ++i) {
-            ts[i].name = r.str();
-            const uint32_t nd = r.get<uint32_t>();
-            if (nd > 4) { r.ok = false; break; }
-            for (uint32_t d = 0; d < nd; ++d) ts[i].ne[d] = int64_t(r.get<uint64_t>());
-            ts[i].type = r.get<uint32_t>();
-            ts[i].offset = r.get<uint64_t>();
-        }
-        if (!r.ok) { rc = fail("truncated GGUF header"); break; }
-        const uint64_t hdr = uint64_t(r.p - base);
-        const uint64_t data = (hdr + alignment - 1) / alignment * alignment;
-        std::unordered_map<std::string, std::string> o2s;
-        load_aliases(map_path ? std::string(map_path) : std::string(path) + ".tensor_map.json", o2s);
-        std::unordered_map<std::string, const GgufTensor*> by_name;
-        for (const auto& t : ts) by_name[t.name] = &t;
-        // Every trunk tensor the file holds, under its original name.
-        std::vector<std::pair<std::string, const GgufTensor*>> want;
-        for (const auto& t : ts) {
-            std::string orig = t.name;
-            for (const auto& kv : o2s)
-                if (kv.second == t.name && kv.first != t.name) { orig = kv.first; break; }
-            if (orig.rfind(kPrefix, 0) == 0) want.emplace_back(orig, &t);
-        }
-        for (const auto& w : want) {
-            const GgufTensor& t = *w.second;
-            int64_t n = t.ne[0] * t.ne[1] * t.ne[2] * t.ne[3];
-            const int64_t nb = type_nbytes(int(t.type), n);
-            if (nb < 0) { rc = fail("unsupported tensor type in " + w.first); break; }
-            if (data + t.offset + uint64_t(nb) > size) { rc = fail("tensor data out of file bounds: " + w.first); break; }
-            if (s3t_set_weight(c, w.first.c_str(), int(t.type), t.ne, base + data + t.offset, size_t(nb))) { rc = -1; break; }
-        }
-    } while (false);
-    munmap(map, size);
-    return rc;
+        if (n_trunk_tensors) *n_trunk_tensors = int(f.trunk.size());
+        if (n_layers) *n_layers = layers;
+        return 0;
+    } S3T_CATCH_INT
 }
 
 int s3t_finalize_weights(s3t_ctx* c) {
-    if (!c) return fail("ctx is null");
-    if (c->finalized) return 0;
-    if (cudaSetDevice(c->device) != cudaSuccess) return fail("cudaSetDevice failed");
-    auto req = [&](const std::string& nm, int64_t e0, int64_t e1, int64_t e2, int64_t e3) -> const Staged* {
-        auto it = c->staged.find(nm);
-        if (it == c->staged.end()) {
-            fail("missing tensor: " + nm);   // src/vision_trunk.cpp:27-33
-            return nullptr;
-        }
-        const Staged& s = it->second;
-        if (s.ne[0] != e0 || s.ne[1] != e1 || s.ne[2] != e2 || s.ne[3] != e3) {
-            fail("unexpected shape for " + nm);
-            return nullptr;
-        }
-        return &s;
-    };
-    const std::string P(kPrefix);
-    int nl = 0;
-    while (nl < kLayers && c->staged.count(P + ".blocks." + std::to_string(nl) + ".attn.qkv.weight")) ++nl;
-    if (nl == 0) return fail("missing tensor: " + P + ".blocks.0.attn.qkv.weight");
-
-    const Staged* pw = req(P + ".patch_embed.proj.weight", 3, 14, 14, 1024);
-    const Staged* pe = req(P + ".pos_embed", 1024, 577, 1, 1);
-    const Staged* lw = req(P + ".ln_pre.weight", 1024, 1, 1, 1);
-    const Staged* lb = req(P + ".ln_pre.bias", 1024, 1, 1, 1);
-    if (!pw || !pe || !lw || !lb) return -1;
-    if (pw->type != S3T_TYPE_F32 && pw->type != S3T_TYPE_F16) return fail("patch_embed must be F32 or F16");
-
-    // Patch-embed weight: GGUF [O][KH][KW][I] -> [O][ic*196 + kh*14 + kw] fp16,
-    // zero padded to 640 columns.
-    {
-        std::vector<__half> wp(size_t(kDim) * kPatchKPad, __float2half(0.f));
-        for (int o = 0; o < kDim; ++o)
-            for (int kh = 0; kh < 14; ++kh)
-                for (int kw = 0; kw < 14; ++kw)
-                    for (int ic = 0; ic < 3; ++ic) {
-                        const size_t src = ((size_t(o) * 14 + kh) * 14 + kw) * 3 + ic;
-                        float v;
-                        if (pw->type == S3T_TYPE_F32) memcpy(&v, pw->host.data() + src * 4, 4);
-                        else v = __half2float(reinterpret_cast<const __half*>(pw->host.data())[src]);
-                        wp[size_t(o) * kPatchKPad + ic * 196 + kh * 14 + kw] = __float2half_rn(v);
-                    }
-        if (dev_alloc(c->allocs, &c->patch_w, wp.size() * 2)) return -1;
-        S3T_CUDA(cudaMemcpy(c->patch_w, wp.data(), wp.size() * 2, cudaMemcpyHostToDevice));
-    }
-    if (upload_f32_vec(c, *pe, 577 * 1024, &c->pos) || upload_f32_vec(c, *lw, 1024, &c->lnpre_w) ||
-        upload_f32_vec(c, *lb, 1024, &c->lnpre_b))
-        return -1;
-
-    for (int l = 0; l < nl; ++l) {
-        const std::string b = P + ".blocks." + std::to_string(l);
-        LayerW& w = c->layers[l];
-        struct Lin { const char* nm; int64_t k, n; __half** dst; int* t; } lins[4] = {
-            {".attn.qkv.weight", kDim, 3 * kDim, &w.qkv, &w.qkv_t},
-            {".attn.proj.weight", kDim, kDim, &w.proj, &w.proj_t},
-            {".mlp.fc1.weight", kDim, kMlp, &w.fc1, &w.fc1_t},
-            {".mlp.fc2.weight", kMlp, kDim, &w.fc2, &w.fc2_t},
+    try {
+        if (!c) return fail("ctx is null");
+        if (c->finalized) return 0;
+        if (cudaSetDevice(c->device) != cudaSuccess) return fail("cudaSetDevice failed");
+        auto req = [&](const std::string& nm, int64_t e0, int64_t e1, int64_t e2, int64_t e3) -> const Staged* {
+            auto it = c->staged.find(nm);
+            if (it == c->staged.end()) {
+                fail("missing tensor: " + nm);   // src/vision_trunk.cpp:27-33
+                return nullptr;
+            }
+            const Staged& s = it->second;
+            if (s.ne[0] != e0 || s.ne[1] != e1 || s.ne[2] != e2 || s.ne[3] != e3) {
+                fail("unexpected shape for " + nm);
+                return nullptr;
+            }
+            return &s;
         };
-        for (auto& li : lins) {
-            const Staged* s = req(b + li.nm, li.k, li.n, 1, 1);
-            if (!s) return -1;
-            *li.t = s->type;
-            const int64_t n = li.k * li.n;
-            if (s->type == S3T_TYPE_F16) {
-                *li.dst = static_cast<__half*>(s->dev);   // already the GEMM operand [N][K]
-                c->allocs.push_back(s->dev);
-                c->staged[b + li.nm].dev = nullptr;
-            } else {
-                if (dev_alloc(c->allocs, li.dst, n * 2)) return -1;
-                if (s->type == S3T_TYPE_Q8_0) S3T_CUDA(launch_dequant_q8_0_to_f16(static_cast<const uint8_t*>(s->dev), n, *li.dst, c->stream));
-                else S3T_CUDA(launch_f32_to_f16(static_cast<const float*>(s->dev), n, *li.dst, c->stream));
+        const std::string P(kPrefix);
+        int nl = 0;
+        while (nl < kLayers && c->staged.count(P + ".blocks." + std::to_string(nl) + ".attn.qkv.weight")) ++nl;
+        if (nl == 0) return fail("missing tensor: " + P + ".blocks.0.attn.qkv.weight");
+
+        const Staged* pw = req(P + ".patch_embed.proj.weight", 3, 14, 14, 1024);
+        const Staged* pe = req(P + ".pos_embed", 1024, 577, 1, 1);
+        const Staged* lw = req(P + ".ln_pre.weight", 1024, 1, 1, 1);
+        const Staged* lb = req(P + ".ln_pre.bias", 1024, 1, 1, 1);
+        if (!pw || !pe || !lw || !lb) return -1;
+        if (pw->type != S3T_TYPE_F32 && pw->type != S3T_TYPE_F16) return fail("patch_embed must be F32 or F16");
+
+        // Patch-embed weight: GGUF [O][KH][KW][I] -> [O][ic*196 + kh*14 + kw] fp16,
+        // zero padded to 640 columns.
+        {
+            std::vector<__half> wp(size_t(kDim) * kPatchKPad, __float2half(0.f));
+            for (int o = 0; o < kDim; ++o)
+                for (int kh = 0; kh < 14; ++kh)
+                    for (int kw = 0; kw < 14; ++kw)
+                        for (int ic = 0; ic < 3; ++ic) {
+                            const size_t src = ((size_t(o) * 14 + kh) * 14 + kw) * 3 + ic;
+                            float v;
+                            if (pw->type == S3T_TYPE_F32) memcpy(&v, pw->host.data() + src * 4, 4);
+                            else v = __half2float(reinterpret_cast<const __half*>(pw->host.data())[src]);
+                            wp[size_t(o) * kPatchKPad + ic * 196 + kh * 14 + kw] = __float2half_rn(v);
+                        }
+            if (dev_alloc(c->allocs, &c->patch_w, wp.size() * 2)) return -1;
+            S3T_CUDA(cudaMemcpy(c->patch_w, wp.data(), wp.size() * 2, cudaMemcpyHostToDevice));
+        }
+        if (upload_f32_vec(c, *pe, 577 * 1024, &c->pos) || upload_f32_vec(c, *lw, 1024, &c->lnpre_w) ||
+            upload_f32_vec(c, *lb, 1024, &c->lnpre_b))
+            return -1;
+
+        for (int l = 0; l < nl; ++l) {
+            const std::string b = P + ".blocks." + std::to_string(l);
+            LayerW& w = c->layers[l];
+            struct Lin { const char* nm; int64_t k, n; __half** dst; int* t; } lins[4] = {
+                {".attn.qkv.weight", kDim, 3 * kDim, &w.qkv, &w.qkv_t},
+                {".attn.proj.weight", kDim, kDim, &w.proj, &w.proj_t},
+                {".mlp.fc1.weight", kDim, kMlp, &w.fc1, &w.fc1_t},
+                {".mlp.fc2.weight", kMlp, kDim, &w.fc2, &w.fc2_t},
+            };
+            for (auto& li : lins) {
+                const Staged* s = req(b + li.nm, li.k, li.n, 1, 1);
+                if (!s) return -1;
+                *li.t = s->type;
+                const int64_t n = li.k * li.n;
+                if (s->type == S3T_TYPE_F16) {
+                    *li.dst = static_cast<__half*>(s->dev);   // already the GEMM operand [N][K]
+                    c->allocs.push_back(s->dev);
+                    c->staged[b + li.nm].dev = nullptr;
+                } else {
+                    if (dev_alloc(c->allocs, li.dst, n * 2)) return -1;
+                    if (s->type == S3T_TYPE_Q8_0) S3T_CUDA(launch_dequant_q8_0_to_f16(static_cast<const uint8_t*>(s->dev), n, *li.dst, c->stream));
+                    else S3T_CUDA(launch_f32_to_f16(static_cast<const float*>(s->dev), n, *li.dst, c->stream));
+                }
+            }
+            struct Vec { const char* nm; int64_t n; float** dst; } vecs[8] = {
+                {".norm1.weight", kDim, &w.n1w}, {".norm1.bias", kDim, &w.n1b},
+                {".attn.qkv.bias", 3 * kDim, &w.qkv_b}, {".attn.proj.bias", kDim, &w.proj_b},
+                {".norm2.weight", kDim, &w.n2w}, {".norm2.bias", kDim, &w.n2b},
+                {".mlp.fc1.bias", kMlp, &w.fc1_b}, {".mlp.fc2.bias", kDim, &w.fc2_b},
+            };
+            for (auto& v : vecs) {
+                const Staged* s = req(b + v.nm, v.n, 1, 1, 1);
+                if (!s || upload_f32_vec(c, *s, v.n, v.dst)) return -1;
             }
         }
-        struct Vec { const char* nm; int64_t n; float** dst; } vecs[8] = {
-            {".norm1.weight", kDim, &w.n1w}, {".norm1.bias", kDim, &w.n1b},
-            {".attn.qkv.bias", 3 * kDim, &w.qkv_b}, {".attn.proj.bias", kDim, &w.proj_b},
-            {".norm2.weight", kDim, &w.n2w}, {".norm2.bias", kDim, &w.n2b},
-            {".mlp.fc1.bias", kMlp, &w.fc1_b}, {".mlp.fc2.bias", kDim, &w.fc2_b},
-        };
-        for (auto& v : vecs) {
-            const Staged* s = req(b + v.nm, v.n, 1, 1, 1);
-            if (!s || upload_f32_vec(c, *s, v.n, v.dst)) return -1;
-        }
-    }
-    S3T_CUDA(cudaStreamSynchronize(c->stream));
-    for (auto& kv : c->staged)
-        if (kv.second.dev) cudaFree(kv.second.dev);
-    c->staged.clear();
-    c->n_layers = nl;
-    c->finalized = true;
-    return 0;
+        S3T_CUDA(cudaStreamSynchronize(c->stream));
+        for (auto& kv : c->staged)
+            if (kv.second.dev) cudaFree(kv.second.dev);
+        c->staged.clear();
+        c->n_layers = nl;
+        c->finalized = true;
+        return 0;
+    } S3T_CATCH_INT
 }
 
 int s3t_num_layers(const s3t_ctx* c) { return c ? c->n_layers : 0; }
 
 int s3t_trunk_run(s3t_ctx* c, const float* images, int batch, float* out, int flags, void* stream) {
-    return run_impl(c, images, batch, c ? c->n_layers : 0, out, flags, stream);
+    try {
+        return run_impl(c, images, batch, c ? c->n_layers : 0, out, flags, stream);
+    } S3T_CATCH_INT
 }
 
 int s3t_trunk_run_layers(s3t_ctx* c, const float* images, int batch, int n_layers, float* out, int flags,
                          void* stream) {
-    return run_impl(c, images, batch, n_layers, out, flags, stream);
+    try {
+        return run_impl(c, images, batch, n_layers, out, flags, stream);
+    } S3T_CATCH_INT
+}
+
+int s3t_trunk_run_block(s3t_ctx* c, int layer, const float* x_dev, int batch, float* out_dev, void* stream) {
+    try {
+        if (!c) return fail("ctx is null");
+        if (!c->finalized) return fail("weights not finalized (call s3t_finalize_weights)");
+        if (!x_dev || !out_dev) return fail("x or out is null");
+        if (batch <= 0) return fail("batch must be positive");
+        if (layer < 0 || layer >= c->n_layers) return fail("layer out of range");
+        S3T_CUDA(cudaSetDevice(c->device));
+        cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+        if (ensure_workspace(c, batch)) return -1;
+        const int M = batch * kTokens;
+        const LayerW& w = c->layers[layer];
+        S3T_CUDA(cudaMemsetAsync(c->dev->status, 0, sizeof(int), st));
+        S3T_CUDA(cudaMemcpyAsync(c->x, x_dev, size_t(M) * kDim * 4, cudaMemcpyDeviceToDevice, st));
+        S3T_CUDA(launch_layernorm(c->x, M, w.n1w, w.n1b, c->a16, w.qkv_t == S3T_TYPE_Q8_0, st));
+        if (enqueue_block(c, layer, batch, nullptr, st)) return -1;
+        S3T_CUDA(cudaMemcpyAsync(out_dev, c->x, size_t(M) * kDim * 4, cudaMemcpyDeviceToDevice, st));
+        return check_status(c, st);
+    } S3T_CATCH_INT
 }
 
 int s3t_trunk_run_rgb8(s3t_ctx* c, const uint8_t* rgb, int width, int height, int batch, float* out, int flags,
                        void* stream) {
-    if (!c) return fail("ctx is null");
-    if (!c->finalized) return fail("weights not finalized (call s3t_finalize_weights)");
-    if (!rgb || !out) return fail("rgb or out is null");
-    if (batch <= 0 || batch > 65535) return fail("batch must be in [1, 65535]");
-    if (width <= 0 || height <= 0 || width > kMaxSourceSide || height > kMaxSourceSide)
-        return fail("image width and height must be in [1, 32768]");
-    S3T_CUDA(cudaSetDevice(c->device));
-    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : c->stream;
-    if (ensure_workspace(c, batch)) return -1;
-    const uint8_t* src = rgb;
-    if (!(flags & S3T_IMAGES_ON_DEVICE)) {
-        const size_t bytes = size_t(batch) * size_t(height) * size_t(width) * 3;
-        if (bytes > c->rgb_cap) {
-            if (c->rgb) {
-                S3T_CUDA(cudaStreamSynchronize(st));
-                S3T_CUDA(cudaFree(c->rgb));
-                c->rgb = nullptr;
-                c->rgb_cap = 0;
+    try {
+        if (!c) return fail("ctx is null");
+        if (!c->finalized) return fail("weights not finalized (call s3t_finalize_weights)");
+        if (!rgb || !out) return fail("rgb or out is null");
+        if (batch <= 0 || batch > 65535) return fail("batch must be in [1, 65535]");
+        if (width <= 0 || height <= 0 || width > kMaxSourceSide || height > kMaxSourceSide)
+            return fail("image width and height must be in [1, 32768]");
+        S3T_CUDA(cudaSetDevice(c->device));
+        cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+        if (ensure_workspace(c, batch)) return -1;
+        const uint8_t* src = rgb;
+        if (!(flags & S3T_IMAGES_ON_DEVICE)) {
+            const size_t bytes = size_t(batch) * size_t(height) * size_t(width) * 3;
+            if (bytes > c->rgb_cap) {
+                if (c->rgb) {
+                    S3T_CUDA(cudaStreamSynchronize(st));
+                    S3T_CUDA(cudaFree(c->rgb));
+                    c->rgb = nullptr;
+                    c->rgb_cap = 0;
+                }
+                void* q = nullptr;
+                const cudaError_t e = cudaMalloc(&q, bytes);
+                if (e != cudaSuccess) return fail("cudaMalloc(" + std::to_string(bytes) + "): " + cudaGetErrorString(e));
+                c->rgb = static_cast<uint8_t*>(q);
+                c->rgb_cap = bytes;
             }
-            void* q = nullptr;
-            const cudaError_t e = cudaMalloc(&q, bytes);
-            if (e != cudaSuccess) return fail("cudaMalloc(" + std::to_string(bytes) + "): " + cudaGetErrorString(e));
-            c->rgb = static_cast<uint8_t*>(q);
-            c->rgb_cap = bytes;
+            S3T_CUDA(cudaMemcpyAsync(c->rgb, rgb, bytes, cudaMemcpyHostToDevice, st));
+            src = c->rgb;
         }
-        S3T_CUDA(cudaMemcpyAsync(c->rgb, rgb, bytes, cudaMemcpyHostToDevice, st));
-        src = c->rgb;
-    }
-    S3T_CUDA(launch_resize_rgb8(src, width, height, batch, c->img, st));
-    return run_impl(c, c->img, batch, c->n_layers, out, flags | S3T_IMAGES_ON_DEVICE, stream);
+        S3T_CUDA(launch_resize_rgb8(src, width, height, batch, c->img, st));
+        return run_impl(c, c->img, batch, c->n_layers, out, flags | S3T_IMAGES_ON_DEVICE, stream);
+    } S3T_CATCH_INT
 }
 
 int s3t_trunk_profile(s3t_ctx* c, const float* images_dev, int batch, float* out_dev, void* stream, double* kind_ms,
                       int* kind_launches) {
-    if (!c) return fail("ctx is null");
-    if (!c->finalized) return fail("weights not finalized (call s3t_finalize_weights)");
-    if (!images_dev || !out_dev || !kind_ms || !kind_launches) return fail("null argument to s3t_trunk_profile");
-    if (batch <= 0) return fail("batch must be positive");
-    S3T_CUDA(cudaSetDevice(c->device));
-    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : c->stream;
-    if (ensure_workspace(c, batch)) return -1;
-    std::vector<std::pair<int, cudaEvent_t>> ev;
-    c->prof = &ev;
-    const int rc = enqueue_trunk(c, images_dev, batch, c->n_layers, out_dev, st);
-    c->prof = nullptr;
-    const cudaError_t se = cudaStreamSynchronize(st);
-    for (int k = 0; k < kProfKinds; ++k) {
-        kind_ms[k] = 0.0;
-        kind_launches[k] = 0;
-    }
-    for (size_t i = 1; rc == 0 && se == cudaSuccess && i < ev.size(); ++i) {
-        float ms = 0.f;
-        if (cudaEventElapsedTime(&ms, ev[i - 1].second, ev[i].second) == cudaSuccess && ev[i].first >= 0) {
-            kind_ms[ev[i].first] += ms;
-            kind_launches[ev[i].first] += 1;
+    try {
+        if (!c) return fail("ctx is null");
+        if (!c->finalized) return fail("weights not finalized (call s3t_finalize_weights)");
+        if (!images_dev || !out_dev || !kind_ms || !kind_launches) return fail("null argument to s3t_trunk_profile");
+        if (batch <= 0) return fail("batch must be positive");
+        S3T_CUDA(cudaSetDevice(c->device));
+        cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+        if (ensure_workspace(c, batch)) return -1;
+        std::vector<std::pair<int, cudaEvent_t>> ev;
+        c->prof = &ev;
+        const int rc = enqueue_trunk(c, images_dev, batch, c->n_layers, out_dev, st);
+        c->prof = nullptr;
+        const cudaError_t se = cudaStreamSynchronize(st);
+        for (int k = 0; k < kProfKinds; ++k) {
+            kind_ms[k] = 0.0;
+            kind_launches[k] = 0;
         }
-    }
-    for (auto& e : ev) cudaEventDestroy(e.second);
-    if (rc) return rc;
-    S3T_CUDA(se);
-    return check_status(c, st);
+        for (size_t i = 1; rc == 0 && se == cudaSuccess && i < ev.size(); ++i) {
+            float ms = 0.f;
+            if (cudaEventElapsedTime(&ms, ev[i - 1].second, ev[i].second) == cudaSuccess && ev[i].first >= 0) {
+                kind_ms[ev[i].first] += ms;
+                kind_launches[ev[i].first] += 1;
+            }
+        }
+        for (auto& e : ev) cudaEventDestroy(e.second);
+        if (rc) return rc;
+        S3T_CUDA(se);
+        return check_status(c, st);
+    } S3T_CATCH_INT
 }
 
 int s3t_sync(s3t_ctx* c, void* stream) {
-    if (!c) return fail("ctx is null");
-    S3T_CUDA(cudaSetDevice(c->device));
-    return check_status(c, stream ? static_cast<cudaStream_t>(stream) : c->stream);
+    try {
+        if (!c) return fail("ctx is null");
+        S3T_CUDA(cudaSetDevice(c->device));
+        return check_status(c, stream ? static_cast<cudaStream_t>(stream) : c->stream);
+    } S3T_CATCH_INT
 }
 
 // ---------------------------------------------------------- op level ---
 
 int s3t_dequantize(int type, const void* src, int64_t n, float* dst, void* stream) {
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (type == S3T_TYPE_Q8_0) {
-        if (n % 32) return fail("Q8_0 length must be a multiple of 32");
-        S3T_CUDA(launch_dequant_q8_0_to_f32(static_cast<const uint8_t*>(src), n, dst, st));
-    } else if (type == S3T_TYPE_F16) {
-        S3T_CUDA(launch_f16_to_f32(static_cast<const __half*>(src), n, dst, st));
-    } else if (type == S3T_TYPE_F32) {
-        S3T_CUDA(cudaMemcpyAsync(dst, src, n * 4, cudaMemcpyDeviceToDevice, st));
-    } else {
-        return fail("unsupported type");
-    }
-    return 0;
+    try {
+        cudaStream_t st = static_cast<cudaStream_t>(stream);
+        if (type == S3T_TYPE_Q8_0) {
+            if (n % 32) return fail("Q8_0 length must be a multiple of 32");
+            S3T_CUDA(launch_dequant_q8_0_to_f32(static_cast<const uint8_t*>(src), n, dst, st));
+        } else if (type == S3T_TYPE_F16) {
+            S3T_CUDA(launch_f16_to_f32(static_cast<const __half*>(src), n, dst, st));
+        } else if (type == S3T_TYPE_F32) {
+            S3T_CUDA(cudaMemcpyAsync(dst, src, n * 4, cudaMemcpyDeviceToDevice, st));
+        } else {
+            return fail("unsupported type");
+        }
+        return 0;
+    } S3T_CATCH_INT
+}
+
+int s3t_weight_operand(int type, const void* src, int64_t n, void* dst16, void* stream) {
+    try {
+        cudaStream_t st = static_cast<cudaStream_t>(stream);
+        if (!src || !dst16 || n <= 0) return fail("weight_operand: null buffer or empty length");
+        if (type == S3T_TYPE_Q8_0) {
+            if (n % 32) return fail("Q8_0 length must be a multiple of 32");
+            S3T_CUDA(launch_dequant_q8_0_to_f16(static_cast<const uint8_t*>(src), n, static_cast<__half*>(dst16), st));
+        } else if (type == S3T_TYPE_F32) {
+            S3T_CUDA(launch_f32_to_f16(static_cast<const float*>(src), n, static_cast<__half*>(dst16), st));
+        } else if (type == S3T_TYPE_F16) {
+            S3T_CUDA(cudaMemcpyAsync(dst16, src, size_t(n) * 2, cudaMemcpyDeviceToDevice, st));
+        } else {
+            return fail("unsupported type");
+        }
+        return 0;
+    } S3T_CATCH_INT
 }
 
 int s3t_gemm_f16(int device, const void* x16, const void* w16, const float* bias, int M, int N, int K, int act, int q8,
                  void* y16, void* stream) {
-    DeviceState* ds = nullptr;
-    if (device_state(device, &ds)) return -1;
-    S3T_CUDA(cudaSetDevice(device));
-    if (K % 64 || N % 32 || M <= 0) return fail("gemm needs K % 64 == 0, N % 32 == 0, M > 0");
-    GemmArgs g{};
-    g.M = M; g.N = N; g.K = K;
-    g.bias = bias;
-    g.out16 = static_cast<__half*>(y16);
-    g.gelu = act == 1;
-    g.q8 = q8;
-    g.status = ds->status;
-    S3T_CUDA(launch_gemm(static_cast<const __half*>(x16), static_cast<const __half*>(w16), g, kEpiF16, ds->num_sms,
-                         static_cast<cudaStream_t>(stream)));
-    return 0;
+    try {
+        DeviceState* ds = nullptr;
+        if (device_state(device, &ds)) return -1;
+        S3T_CUDA(cudaSetDevice(device));
+        if (K % 64 || N % 32 || M <= 0) return fail("gemm needs K % 64 == 0, N % 32 == 0, M > 0");
+        GemmArgs g{};
+        g.M = M; g.N = N; g.K = K;
+        g.bias = bias;
+        g.out16 = static_cast<__half*>(y16);
+        g.gelu = act == 1;
+        g.q8 = q8;
+        g.status = ds->status;
+        S3T_CUDA(launch_gemm(static_cast<const __half*>(x16), static_cast<const __half*>(w16), g, kEpiF16, ds->num_sms,
+                             static_cast<cudaStream_t>(stream)));
+        return 0;
+    } S3T_CATCH_INT
 }
 
 int s3t_attention(int device, const void* q, const void* k, const void* v, int groups, int L, int windowed, int bf16,
                   void* out, void* stream) {
-    DeviceState* ds = nullptr;
-    if (device_state(device, &ds)) return -1;
-    S3T_CUDA(cudaSetDevice(device));
-    if (L % 64 || groups <= 0) return fail("attention needs L % 64 == 0 and groups > 0");
-    if (windowed ? (L != kWindow * kWindow || groups % 9) : (L != kTokens))
-        return fail("attention output mapping needs L = 576 (windowed, groups = 9*images) or 5184 (global)");
-    AttnArgs a{};
-    a.q = q; a.k = k; a.v = v;
-    a.groups = groups; a.L = L; a.windowed = windowed;
-    a.scale_log2 = 0.125f * 1.4426950408889634f;
-    a.bf16 = bf16;
-    a.out = out;
-    a.status = ds->status;
-    S3T_CUDA(launch_attention(a, static_cast<cudaStream_t>(stream)));
-    return 0;
+    try {
+        DeviceState* ds = nullptr;
+        if (device_state(device, &ds)) return -1;
+        S3T_CUDA(cudaSetDevice(device));
+        if (L % 64 || groups <= 0) return fail("attention needs L % 64 == 0 and groups > 0");
+        if (windowed ? (L != kWindow * kWindow || groups % 9) : (L != kTokens))
+            return fail("attention output mapping needs L = 576 (windowed, groups = 9*images) or 5184 (global)");
+        AttnArgs a{};
+        a.q = q; a.k = k; a.v = v;
+        a.groups = groups; a.L = L; a.windowed = windowed;
+        a.scale_log2 = 0.125f * 1.4426950408889634f;
+        a.bf16 = bf16;
+        a.out = out;
+        a.status = ds->status;
+        S3T_CUDA(launch_attention(a, static_cast<cudaStream_t>(stream)));
+        return 0;
+    } S3T_CATCH_INT
 }
 
 int s3t_mha_d32(int device, const void* q, const void* k, const void* v, int batch, int q_len, int kv_len,
                 const float* key_mask, void* out, int flags, void* stream) {
-    DeviceState* ds = nullptr;
-    if (device_state(device, &ds)) return -1;
-    S3T_CUDA(cudaSetDevice(device));
-    if (!q || !k || !v || !out) return fail("mha_d32: q, k, v and out must be device pointers");
-    if (batch <= 0 || q_len <= 0 || kv_len <= 0) return fail("mha_d32 needs batch, q_len and kv_len > 0");
-    if (int64_t(batch) * (q_len + 127) / 128 * 8 > (int64_t(1) << 30)) return fail("mha_d32: batch * q_len too large");
-    if (flags & ~(S3T_MHA_BF16 | S3T_MHA_OUT_F16 | S3T_MHA_BIAS)) return fail("mha_d32: unknown flags");
-    if ((flags & S3T_MHA_BIAS) && !key_mask) return fail("mha_d32: S3T_MHA_BIAS needs the bias array");
-    if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
-         reinterpret_cast<uintptr_t>(out)) & 15)
-        return fail("mha_d32: q, k, v and out must be 16-byte aligned");
-    MhaArgs a{};
-    a.q = q; a.k = k; a.v = v;
-    a.key_mask = key_mask;
-    a.batch = batch;
-    a.q_len = q_len; a.kv_len = kv_len;
-    // The reference's scale, 1.0f / std::sqrt(float(kHeadDim)), in the log2 domain.
-    a.scale_log2 = (1.0f / std::sqrt(32.0f)) * 1.4426950408889634f;
-    a.bf16 = (flags & S3T_MHA_BF16) != 0;
-    a.out_f16 = (flags & S3T_MHA_OUT_F16) != 0;
-    a.bias = (flags & S3T_MHA_BIAS) != 0;
-    a.out = out;
-    a.status = ds->status;
-    S3T_CUDA(launch_mha32(a, static_cast<cudaStream_t>(stream)));
-    return 0;
+    try {
+        DeviceState* ds = nullptr;
+        if (device_state(device, &ds)) return -1;
+        S3T_CUDA(cudaSetDevice(device));
+        if (!q || !k || !v || !out) return fail("mha_d32: q, k, v and out must be device pointers");
+        if (batch <= 0 || q_len <= 0 || kv_len <= 0) return fail("mha_d32 needs batch, q_len and kv_len > 0");
+        if (int64_t(batch) * (q_len + 127) / 128 * 8 > (int64_t(1) << 30)) return fail("mha_d32: batch * q_len too large");
+        if (flags & ~(S3T_MHA_BF16 | S3T_MHA_OUT_F16 | S3T_MHA_BIAS)) return fail("mha_d32: unknown flags");
+        if ((flags & S3T_MHA_BIAS) && !key_mask) return fail("mha_d32: S3T_MHA_BIAS needs the bias array");
+        if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
+             reinterpret_cast<uintptr_t>(out)) & 15)
+            return fail("mha_d32: q, k, v and out must be 16-byte aligned");
+        MhaArgs a{};
+        a.q = q; a.k = k; a.v = v;
+        a.key_mask = key_mask;
+        a.batch = batch;
+        a.q_len = q_len; a.kv_len = kv_len;
+        // The reference's scale, 1.0f / std::sqrt(float(kHeadDim)), in the log2 domain.
+        a.scale_log2 = (1.0f / std::sqrt(32.0f)) * 1.4426950408889634f;
+        a.bf16 = (flags & S3T_MHA_BF16) != 0;
+        a.out_f16 = (flags & S3T_MHA_OUT_F16) != 0;
+        a.bias = (flags & S3T_MHA_BIAS) != 0;
+        a.out = out;
+        a.status = ds->status;
+        S3T_CUDA(launch_mha32(a, static_cast<cudaStream_t>(stream)));
+        return 0;
+    } S3T_CATCH_INT
 }
 
 int s3t_rope(int device, void* x, int groups, int L, int windowed, int bf16, void* stream) {
-    DeviceState* ds = nullptr;
-    if (device_state(device, &ds)) return -1;
-    S3T_CUDA(cudaSetDevice(device));
-    S3T_CUDA(launch_rope_inplace(x, groups, L, windowed, bf16, ds->rope_local, ds->rope_global,
-                                 static_cast<cudaStream_t>(stream)));
-    return 0;
+    try {
+        DeviceState* ds = nullptr;
+        if (device_state(device, &ds)) return -1;
+        S3T_CUDA(cudaSetDevice(device));
+        S3T_CUDA(launch_rope_inplace(x, groups, L, windowed, bf16, ds->rope_local, ds->rope_global,
+                                     static_cast<cudaStream_t>(stream)));
+        return 0;
+    } S3T_CATCH_INT
 }
 
 int s3t_layernorm(int device, const float* x, int rows, const float* gamma, const float* beta, void* y16, int q8,
                   void* stream) {
-    DeviceState* ds = nullptr;
-    if (device_state(device, &ds)) return -1;
-    S3T_CUDA(cudaSetDevice(device));
-    S3T_CUDA(launch_layernorm(x, rows, gamma, beta, static_cast<__half*>(y16), q8, static_cast<cudaStream_t>(stream)));
-    return 0;
+    try {
+        DeviceState* ds = nullptr;
+        if (device_state(device, &ds)) return -1;
+        S3T_CUDA(cudaSetDevice(device));
+        S3T_CUDA(launch_layernorm(x, rows, gamma, beta, static_cast<__half*>(y16), q8, static_cast<cudaStream_t>(stream)));
+        return 0;
+    } S3T_CATCH_INT
 }
 
 int s3t_preprocess_rgb8(int device, const uint8_t* rgb, int width, int height, int batch, float* out, void* stream) {
-    DeviceState* ds = nullptr;
-    if (device_state(device, &ds)) return -1;
-    if (!rgb || !out) return fail("rgb or out is null");
-    if (batch <= 0 || batch > 65535) return fail("batch must be in [1, 65535]");
-    if (width <= 0 || height <= 0 || width > kMaxSourceSide || height > kMaxSourceSide)
-        return fail("image width and height must be in [1, 32768]");
-    S3T_CUDA(cudaSetDevice(device));
-    S3T_CUDA(launch_resize_rgb8(rgb, width, height, batch, out, static_cast<cudaStream_t>(stream)));
-    return 0;
+    try {
+        DeviceState* ds = nullptr;
+        if (device_state(device, &ds)) return -1;
+        if (!rgb || !out) return fail("rgb or out is null");
+        if (batch <= 0 || batch > 65535) return fail("batch must be in [1, 65535]");
+        if (width <= 0 || height <= 0 || width > kMaxSourceSide || height > kMaxSourceSide)
+            return fail("image width and height must be in [1, 32768]");
+        S3T_CUDA(cudaSetDevice(device));
+        S3T_CUDA(launch_resize_rgb8(rgb, width, height, batch, out, static_cast<cudaStream_t>(stream)));
+        return 0;
+    } S3T_CATCH_INT
 }
 
 int s3t_selftest_wait_timeout(int device, int limit_ms) {
-    DeviceState* ds = nullptr;
-    if (device_state(device, &ds)) return -1;
-    if (limit_ms < 1 || limit_ms > 2000) return fail("limit_ms must be in [1, 2000]");
-    S3T_CUDA(cudaSetDevice(device));
-    int* gave_up = nullptr;
-    S3T_CUDA(cudaMalloc(&gave_up, sizeof(int)));
-    S3T_CUDA(cudaMemset(gave_up, 0, sizeof(int)));
-    cudaError_t e = launch_wait_timeout_probe(ds->status, uint64_t(limit_ms) * 1000000ull, gave_up, nullptr);
-    if (e == cudaSuccess) e = cudaDeviceSynchronize();
-    int h = 0;
-    if (e == cudaSuccess) e = cudaMemcpy(&h, gave_up, sizeof(int), cudaMemcpyDeviceToHost);
-    cudaFree(gave_up);
-    S3T_CUDA(e);
-    if (!h) return fail("self-test: the bounded wait did not give up");
-    return 0;   // the timeout is now in the device status word (s3t_device_status reports it)
+    try {
+        DeviceState* ds = nullptr;
+        if (device_state(device, &ds)) return -1;
+        if (limit_ms < 1 || limit_ms > 2000) return fail("limit_ms must be in [1, 2000]");
+        S3T_CUDA(cudaSetDevice(device));
+        int* gave_up = nullptr;
+        S3T_CUDA(cudaMalloc(&gave_up, sizeof(int)));
+        S3T_CUDA(cudaMemset(gave_up, 0, sizeof(int)));
+        cudaError_t e = launch_wait_timeout_probe(ds->status, uint64_t(limit_ms) * 1000000ull, gave_up, nullptr);
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
+        int h = 0;
+        if (e == cudaSuccess) e = cudaMemcpy(&h, gave_up, sizeof(int), cudaMemcpyDeviceToHost);
+        cudaFree(gave_up);
+        S3T_CUDA(e);
+        if (!h) return fail("self-test: the bounded wait did not give up");
+        return 0;   // the timeout is now in the device status word (s3t_device_status reports it)
+    } S3T_CATCH_INT
 }
 
 int s3t_device_status(int device) {
-    DeviceState* ds = nullptr;
-    if (device_state(device, &ds)) return -1;
-    S3T_CUDA(cudaSetDevice(device));
-    S3T_CUDA(cudaDeviceSynchronize());
-    int code = 0;
-    S3T_CUDA(cudaMemcpy(&code, ds->status, sizeof(int), cudaMemcpyDeviceToHost));
-    S3T_CUDA(cudaMemset(ds->status, 0, sizeof(int)));
-    if (code) return fail(std::string("device error: ") + status_message(code));
-    return 0;
+    try {
+        DeviceState* ds = nullptr;
+        if (device_state(device, &ds)) return -1;
+        S3T_CUDA(cudaSetDevice(device));
+        S3T_CUDA(cudaDeviceSynchronize());
+        int code = 0;
+        S3T_CUDA(cudaMemcpy(&code, ds->status, sizeof(int), cudaMemcpyDeviceToHost));
+        S3T_CUDA(cudaMemset(ds->status, 0, sizeof(int)));
+        if (code) return fail(std::string("device error: ") + status_message(code));
+        return 0;
+    } S3T_CATCH_INT
 }
 
 }  // extern "C"

@@ -9,6 +9,7 @@ sam3::VisionTrunk::run for the full-trunk outputs — on seeded inputs.
     python tests/golden/make_golden.py --ops-only
     python tests/golden/make_golden.py --preprocess-only
     python tests/golden/make_golden.py --mha-only
+    python tests/golden/make_golden.py --blocks-only
 
 Files:
   ops.npz                   inputs and ggml outputs of small op cases
@@ -21,6 +22,12 @@ Files:
   mha_d32_decoder.npz       mha() of src/decoder.cpp:95-127 (mul_mat, soft_max_ext
                             with the prompt mask or the box bias, mul_mat) run by
                             ggml on seeded fp16-exact inputs: DECODER_CASES
+  block_pin_<fmt>.npz       VisionTrunk::run on a file whose blocks other than k
+                            (k in PIN_BLOCKS) are exact identities (all their
+                            weights and biases zero): the reference's own
+                            block_k(stem(image 0)), every PIN_STRIDE-th element
+                            of the NCHW output; pins the harness's per-block
+                            graphs (oracle/ref_harness.cpp ref_trunk_block)
   preprocess.json           the reference tool's bilinear_resize_rgb
                             (tools/sam3_vision_trunk.cpp:33-66) on seeded uint8
                             images of PREPROCESS_SIZES: sha256 of the fp32
@@ -45,6 +52,8 @@ from oracle.pyoracle import F16, F32, Q8_0, Reference  # noqa: E402
 from sam3cpp_b200 import synthetic as s  # noqa: E402
 
 STRIDE = 61
+PIN_STRIDE = 211
+PIN_BLOCKS = (0, 7)   # a windowed block and the first global one
 
 # (height, width) of the seeded uint8 RGB test images: identity size,
 # upsampling, downsampling, degenerate and odd sizes.  Image i is
@@ -224,6 +233,46 @@ def trunk_golden(ref: Reference, fmt: str, threads: int) -> dict:
     }
 
 
+def isolated_block_weights(k: int) -> dict[str, np.ndarray]:
+    """The seeded 32-block weights with every block but k made an exact
+    identity: a block whose weights and biases are all zero adds 0 to the
+    residual twice (attention output 0 through proj, GELU(0) = 0 through fc2).
+    Blocks 0..7 of the seeded files equal those of the seeded 8-layer file
+    (same draws in the same order), which the pin test runs."""
+    w = s.make_f32_weights(0, layers=8)
+    full = s.make_f32_weights(0, layers=0)
+    for i in range(s.LAYERS):
+        b = f"{s.PREFIX}.blocks.{i}"
+        for name, shape in (("attn.qkv", (3 * s.DIM, s.DIM)), ("attn.proj", (s.DIM, s.DIM)),
+                            ("mlp.fc1", (s.MLP, s.DIM)), ("mlp.fc2", (s.DIM, s.MLP))):
+            if i == k:
+                full[f"{b}.{name}.weight"] = w[f"{b}.{name}.weight"]
+                full[f"{b}.{name}.bias"] = w[f"{b}.{name}.bias"]
+            else:
+                full[f"{b}.{name}.weight"] = np.zeros(shape, np.float32)
+                full[f"{b}.{name}.bias"] = np.zeros(shape[0], np.float32)
+        for nm in ("norm1", "norm2"):
+            full[f"{b}.{nm}.weight"] = np.ones(s.DIM, np.float32)
+            full[f"{b}.{nm}.bias"] = np.zeros(s.DIM, np.float32)
+    return full
+
+
+def block_pin_golden(ref: Reference, fmt: str, threads: int) -> dict:
+    import tempfile
+    out = {"stride": np.int64(PIN_STRIDE), "blocks": np.array(PIN_BLOCKS, np.int64)}
+    img = s.synthetic_image(0)
+    with tempfile.TemporaryDirectory() as d:
+        for k in PIN_BLOCKS:
+            path = s.write_gguf(Path(d) / f"isolated_{k}.gguf", isolated_block_weights(k), fmt)
+            y, _ = ref.trunk(path, img, threads)
+            flat = y.reshape(-1)
+            out[f"block{k}_sample"] = flat[::PIN_STRIDE].astype(np.float32)
+            out[f"block{k}_mean"] = np.float64(flat.astype(np.float64).mean())
+            out[f"block{k}_std"] = np.float64(flat.astype(np.float64).std())
+            path.unlink()
+    return out
+
+
 def isa_spread(fmt: str, threads: int, gold: dict) -> dict:
     """Distance between two builds of the same reference code on the same file:
     the AVX2 build (libsam3ref_v3) against the golden AVX-512 build (v4).
@@ -243,10 +292,16 @@ def main():
     ap.add_argument("--ops-only", action="store_true")
     ap.add_argument("--preprocess-only", action="store_true")
     ap.add_argument("--mha-only", action="store_true")
+    ap.add_argument("--blocks-only", action="store_true")
     ap.add_argument("--formats", default="f16,q8_0,f32")
     ap.add_argument("--threads", type=int, default=8)
     a = ap.parse_args()
     ref = Reference()
+    if a.blocks_only:
+        for fmt in a.formats.split(","):
+            np.savez_compressed(HERE / f"block_pin_{fmt}.npz", **block_pin_golden(ref, fmt, a.threads))
+            print(f"block_pin_{fmt}.npz written", flush=True)
+        return
     np.savez_compressed(HERE / "mha_d32.npz", **mha_golden(ref))
     np.savez_compressed(HERE / "mha_d32_decoder.npz", **decoder_golden(ref))
     print("mha_d32.npz, mha_d32_decoder.npz written")

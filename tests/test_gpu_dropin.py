@@ -28,3 +28,21 @@ def test_reference_loader_with_dropin_trunk(torch_cuda):
     # a second run reuses the cached device context of the same GgufModel path
     got2, _ = ref.trunk(s.synthetic_gguf("f16"), s.synthetic_image(0))
     assert np.array_equal(got, got2)
+
+
+@pytest.mark.skipif(not LIB.exists(), reason="oracle/_ref/libsam3ref_s3t.so not built (make -C oracle dropin)")
+def test_dropin_models_loaded_in_sequence_use_their_own_weights(torch_cuda):
+    """ref_trunk_run loads a fresh GgufModel on its stack for every call, so
+    consecutive models of different files usually share one address: each
+    must still run on its own weights (the context cache is keyed by the
+    loaded weights, not by the address alone)."""
+    import sam3cpp_b200 as s3t
+    from oracle.pyoracle import Reference
+    from sam3cpp_b200 import synthetic as s
+    ref = Reference(LIB)
+    img = s.synthetic_image(1)
+    for fmt in ("f16", "q8_0", "f16"):
+        path = s.synthetic_gguf(fmt)
+        got, _ = ref.trunk(path, img)
+        own = s3t.VisionTrunk(s3t.GgufModel(path)).run(img.reshape(-1), [1, 3, 1008, 1008]).trunk_nchw
+        assert np.array_equal(got, own), fmt

@@ -87,8 +87,10 @@ def test_layernorm(s3t, torch_cuda, oracle, q8):
 
 
 def test_dequant_bit_exact(s3t, torch_cuda, oracle):
-    """Device dequantization of Q8_0 and F16 file bytes is bit-identical to
-    ggml's dequantize_row_q8_0 / fp16->fp32 (restated by the oracle)."""
+    """The file-format dequantization on the device (s3t_dequantize, to fp32)
+    is bit-identical to ggml's dequantize_row_q8_0 / fp16->fp32 (restated by
+    the oracle).  This proves the decoding of the GGUF bytes; the operand the
+    trunk's GEMMs consume is checked by test_gemm_weight_operand_bit_exact."""
     torch = torch_cuda
     from sam3cpp_b200.synthetic import quantize_q8_0_rows
     rng = np.random.default_rng(9)
@@ -107,6 +109,39 @@ def test_dequant_bit_exact(s3t, torch_cuda, oracle):
     _ok(s3t, s3t.s3t_dequantize(F16, _p(hd), n, _p(yd), None))
     torch.cuda.synchronize()
     assert np.array_equal(yd.cpu().numpy().view(np.uint32), oracle.dequantize(F16, h.view(np.uint16), n).view(np.uint32))
+
+
+def test_gemm_weight_operand_bit_exact(s3t, torch_cuda):
+    """The fp16 operand the trunk's GEMMs consume (s3t_weight_operand, the
+    conversion s3t_finalize_weights applies): for Q8_0 it is fp16(q*d), the
+    exact product of dequantize_row_q8_0 rounded to nearest even fp16 -- not
+    q*d itself, which needs up to 19 significant bits; for F32 it is the
+    round-to-nearest-even fp16 of the weight; F16 weights pass unchanged."""
+    torch = torch_cuda
+    from sam3cpp_b200.synthetic import quantize_q8_0_rows
+    rng = np.random.default_rng(10)
+    w = (rng.standard_normal((256, 1024)) * 0.02).astype(np.float32)
+    w[3, :32] = 0.0
+    w[7, 5] = 10.0
+    w[9, 64:96] = np.linspace(-1e-3, 1e-3, 32)   # scale d in the fp16 subnormal range
+    n = w.size
+    raw = quantize_q8_0_rows(w)
+    d = raw.reshape(-1, 34)[:, :2].copy().view(np.float16).astype(np.float64)
+    q = raw.reshape(-1, 34)[:, 2:].view(np.int8).astype(np.float64)
+    expect = (q * d).reshape(-1).astype(np.float16)          # float64 -> fp16 rounds to nearest even
+    out = torch.empty(n, dtype=torch.float16, device="cuda")
+    src = torch.from_numpy(raw.reshape(-1)).cuda()
+    _ok(s3t, s3t.s3t_weight_operand(Q8_0, _p(src), n, _p(out), None))
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy().view(np.uint16), expect.view(np.uint16))
+    src = torch.from_numpy(w.reshape(-1)).cuda()
+    _ok(s3t, s3t.s3t_weight_operand(F32, _p(src), n, _p(out), None))
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy().view(np.uint16), w.reshape(-1).astype(np.float16).view(np.uint16))
+    h = torch.from_numpy(w.reshape(-1).astype(np.float16)).cuda()
+    _ok(s3t, s3t.s3t_weight_operand(F16, _p(h), n, _p(out), None))
+    torch.cuda.synchronize()
+    assert torch.equal(out, h)
 
 
 def _grouped_to_oracle(a, groups, L):
