@@ -204,8 +204,9 @@ int s3t_device_status(int device);
  * tiled position embedding + ln_pre for one image, the same values as
  * s3t_trunk_run_layers(ctx, ..., n_layers = 0, ...) but token-major:
  * images_dev [batch][3][1008][1008] fp32 -> out_tokens_dev [batch*5184][1024]
- * fp32, both device pointers on the context's GPU, enqueued on `stream`
- * (NULL = the legacy default stream).  For callers that cannot call
+ * fp32, both device pointers on the context's GPU and 16-byte aligned,
+ * enqueued on `stream` (NULL = the context's own stream, as for every other
+ * entry point that takes a context).  For callers that cannot call
  * cudaMalloc (plugins whose host application owns all device memory, loops
  * with a fixed memory budget): it allocates nothing; its one scratch buffer
  * is a static device array inside the library sized for batch <= 1

@@ -142,6 +142,7 @@ struct StemView {
     const float* ln_w;
     const float* ln_b;
     int* status;
+    cudaStream_t stream;     // the context's own stream
 };
 
 // Tensor-map creation through the driver entry point.

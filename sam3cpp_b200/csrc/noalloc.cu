@@ -92,36 +92,61 @@ __global__ void __launch_bounds__(256) ln_inplace_kernel(float* __restrict__ x, 
     }
 }
 
+// 0 if p is device (or managed) memory of `device`; otherwise the message.
+int check_device_pointer(const void* p, int device, const char* what) {
+    cudaPointerAttributes a{};
+    const cudaError_t e = cudaPointerGetAttributes(&a, p);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return set_last_error((std::string(what) + " is not a CUDA pointer").c_str());
+    }
+    if ((a.type != cudaMemoryTypeDevice && a.type != cudaMemoryTypeManaged) || a.device != device)
+        return set_last_error((std::string(what) + " is not device memory of the context's GPU " +
+                               std::to_string(device)).c_str());
+    return 0;
+}
+
 }  // namespace
 
 extern "C" int s3t_stem_noalloc(s3t_ctx* ctx, const float* images_dev, int batch, float* out_tokens_dev, void* stream) {
-    StemView w;
-    if (!ctx_stem_view(ctx, &w)) return set_last_error("ctx is null or its weights are not finalized");
-    if (!images_dev || !out_tokens_dev) return set_last_error("images or out is null");
-    if (batch < 1 || batch > kStaticImages)
-        return set_last_error(("s3t_stem_noalloc: batch " + std::to_string(batch) + " is outside 1.." +
-                               std::to_string(kStaticImages) + " (its static scratch holds " +
-                               std::to_string(kStaticImages) + " image)").c_str());
-    cudaError_t e = cudaSetDevice(w.device);
-    if (e != cudaSuccess) return set_last_error(cudaGetErrorString(e));
-    __half* patches = nullptr;
-    if (static_patches(w.device, &patches)) return -1;
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
-    const int M = batch * kTokens;
+    try {
+        StemView w;
+        if (!ctx_stem_view(ctx, &w)) return set_last_error("ctx is null or its weights are not finalized");
+        if (!images_dev || !out_tokens_dev) return set_last_error("images or out is null");
+        // The patch gather reads the image and the GEMM epilogue and ln_pre
+        // write the tokens with 16-byte vector accesses.
+        if ((reinterpret_cast<uintptr_t>(images_dev) | reinterpret_cast<uintptr_t>(out_tokens_dev)) & 15)
+            return set_last_error("s3t_stem_noalloc: images and out must be 16-byte aligned");
+        if (batch < 1 || batch > kStaticImages)
+            return set_last_error(("s3t_stem_noalloc: batch " + std::to_string(batch) + " is outside 1.." +
+                                   std::to_string(kStaticImages) + " (its static scratch holds " +
+                                   std::to_string(kStaticImages) + " image)").c_str());
+        cudaError_t e = cudaSetDevice(w.device);
+        if (e != cudaSuccess) return set_last_error(cudaGetErrorString(e));
+        if (check_device_pointer(images_dev, w.device, "images") ||
+            check_device_pointer(out_tokens_dev, w.device, "out"))
+            return -1;
+        __half* patches = nullptr;
+        if (static_patches(w.device, &patches)) return -1;
+        cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : w.stream;
+        const int M = batch * kTokens;
 
-    if ((e = launch_im2col(images_dev, batch, patches, st)) != cudaSuccess)
-        return set_last_error((std::string("im2col: ") + cudaGetErrorString(e)).c_str());
-    GemmArgs g{};
-    g.M = M;
-    g.N = kDim;
-    g.K = kPatchKPad;
-    g.resid = out_tokens_dev;
-    g.pos = w.pos;
-    g.status = w.status;
-    if ((e = launch_gemm(patches, w.patch_w, g, kEpiPatch, w.num_sms, st)) != cudaSuccess)
-        return set_last_error((std::string("patch GEMM: ") + cudaGetErrorString(e)).c_str());
-    ln_inplace_kernel<<<(M + 7) / 8, 256, 0, st>>>(out_tokens_dev, M, w.ln_w, w.ln_b);
-    if ((e = cudaGetLastError()) != cudaSuccess)
-        return set_last_error((std::string("ln_pre: ") + cudaGetErrorString(e)).c_str());
-    return 0;
+        if ((e = launch_im2col(images_dev, batch, patches, st)) != cudaSuccess)
+            return set_last_error((std::string("im2col: ") + cudaGetErrorString(e)).c_str());
+        GemmArgs g{};
+        g.M = M;
+        g.N = kDim;
+        g.K = kPatchKPad;
+        g.resid = out_tokens_dev;
+        g.pos = w.pos;
+        g.status = w.status;
+        if ((e = launch_gemm(patches, w.patch_w, g, kEpiPatch, w.num_sms, st)) != cudaSuccess)
+            return set_last_error((std::string("patch GEMM: ") + cudaGetErrorString(e)).c_str());
+        ln_inplace_kernel<<<(M + 7) / 8, 256, 0, st>>>(out_tokens_dev, M, w.ln_w, w.ln_b);
+        if ((e = cudaGetLastError()) != cudaSuccess)
+            return set_last_error((std::string("ln_pre: ") + cudaGetErrorString(e)).c_str());
+        return 0;
+    } catch (...) {
+        return set_last_error("s3t_stem_noalloc: internal error");
+    }
 }

@@ -753,6 +753,7 @@ bool s3t::ctx_stem_view(const s3t_ctx* c, StemView* out) {
     out->ln_w = c->lnpre_w;
     out->ln_b = c->lnpre_b;
     out->status = c->dev->status;
+    out->stream = c->stream;
     return true;
 }
 
