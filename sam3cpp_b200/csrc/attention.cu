@@ -267,10 +267,9 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
 
                 float acc[8];
 #pragma unroll
-                for (int i = 0; i < 8; ++i)
-                    acc[i] = fmax3(__uint_as_float(r[i]), __uint_as_float(r[8 + i]), __uint_as_float(r[16 + i]));
+                for (int i = 0; i < 8; ++i) acc[i] = fmaxf(__uint_as_float(r[i]), __uint_as_float(r[8 + i]));
 #pragma unroll
-                for (int i = 24; i < 64; i += 16)
+                for (int i = 16; i < 64; i += 16)
 #pragma unroll
                     for (int k = 0; k < 8; ++k)
                         acc[k] = fmax3(acc[k], __uint_as_float(r[i + k]), __uint_as_float(r[i + 8 + k]));

@@ -481,7 +481,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfgT<BK>::THREAD
     uint64_t* tfull = empty + STAGES;
     uint64_t* tempty = tfull + 2;
     uint64_t* drain = tempty + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    uint64_t* rload = drain + 1;                     // [EPI_WARPS]: residual chunk loads (kEpiResid)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rload + Cfg::EPI_WARPS);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -502,6 +503,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfgT<BK>::THREAD
             mbar_init(tempty + i, 2 * Cfg::EPI_WARPS);   // every epilogue warp of the pair
         }
         mbar_init(drain, 1);
+        for (int i = 0; i < Cfg::EPI_WARPS; ++i) mbar_init(rload + i, 1);
         *abort_flag = 0;
         fence_barrier_init();
     }
@@ -609,28 +611,33 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfgT<BK>::THREAD
         const int quarter = warp & 3;
         const int col_grp = (warp - 2) >> 2;
         const int row = quarter * 32 + lane;
+        uint32_t rphase = 0;     // parity of this warp's next residual load
+        bool rpending = false;   // a residual load of this warp is in flight
         int local = 0;
         for (int tile = pair; tile < n_tiles; tile += n_pairs, ++local) {
             const int acc = local & 1;
             const uint32_t aph = (local >> 1) & 1;
             const int m = (tile / n_tiles_n) * 2 * kBM + int(rank) * kBM + row;
             const int n0 = (tile % n_tiles_n) * BN + col_grp * Cfg::WARP_COLS;
-            // kEpiResid: this row's fp32 residual for the first two 32-column
-            // chunks is loaded while the tile's mainloop is still running, the
-            // rest two chunks ahead of use (the residual is not written by
-            // anyone else before this epilogue).
-            float4 xres[2][8];
             const bool row_ok = m < args.M;
             if constexpr (EPI == kEpiResid) {
-                const float4* xr = reinterpret_cast<const float4*>(args.resid + int64_t(m) * args.N + n0);
+                // The fp32 residual comes in by TMA, one 32 x 32 chunk at a time,
+                // into this warp's store stage: the first chunk while the tile's
+                // mainloop still runs, the others pulled into L2 now and loaded
+                // as soon as the previous chunk's store has read the stage (the
+                // residual is not written by anyone else before this epilogue).
+                const int row0 = m - lane;
+                if (*abort_flag) break;
+                if (row0 < args.M) {
+                    if (lane == 0) {
+                        bulk_wait_group_read<0>();
+                        mbar_arrive_expect_tx(rload + (warp - 2), 32 * 32 * 4);
+                        tma_load_2d(sOut + (warp - 2) * Cfg::OUT_BYTES, &tmC, rload + (warp - 2), n0, row0);
 #pragma unroll
-                for (int cc = 0; cc < 2; ++cc)
-#pragma unroll
-                    for (int q = 0; q < 8; ++q)
-                        xres[cc][q] = row_ok ? xr[cc * 8 + q] : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-                for (int q = 2; q < Cfg::WARP_COLS / 32; ++q)
-                    if (row_ok) prefetch_l2(args.resid + int64_t(m) * args.N + n0 + 32 * q);
+                        for (int q = 1; q < Cfg::WARP_COLS / 32; ++q) tma_prefetch_l2_2d(&tmC, n0 + 32 * q, row0);
+                    }
+                    rpending = true;
+                }
             }
             if (!mbar_wait(tfull + acc, aph, args.status, kErrTimeoutEpilogue, abort_flag)) break;
             tc_fence_after();
@@ -708,23 +715,33 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfgT<BK>::THREAD
                     }
                 }
             } else if constexpr (EPI == kEpiResid) {
-                static_assert(Cfg::WARP_COLS % 64 == 0, "chunks come in pairs");
-                // The updated rows leave through a 4 KB shared-memory stage
-                // (32 rows x 128 B, 128-byte swizzle) and one TMA store per chunk.
+                // The stage (32 rows x 128 B, 128-byte swizzle, the layout TMA
+                // writes) holds chunk c of the residual; each lane adds its row's
+                // accumulator and bias in place, and one TMA store writes the
+                // chunk back.  Rows past M are zero-filled by the load and not
+                // written by the store.
                 uint8_t* stage = sOut + (warp - 2) * Cfg::OUT_BYTES;
                 const int row0 = m - lane;
+                const bool chunk_rows = row0 < args.M;   // warp-uniform
+                // A warp whose 32 rows all lie past M has nothing to add or store;
+                // it must not touch the stage, which its previous tile's last
+                // store may still be reading.
 #pragma unroll
-                for (int c = 0; c < Cfg::WARP_COLS / 32; ++c) {
+                for (int c = 0; c < Cfg::WARP_COLS / 32 && chunk_rows; ++c) {
                     const int n = n0 + c * 32;
                     uint32_t r[32];
                     tmem_ld32(tbase + c * 32, r);
                     tmem_wait_ld();
-                    float4(&xc)[8] = xres[c & 1];
+                    if (!mbar_wait(rload + (warp - 2), rphase, args.status, kErrTimeoutEpilogue, abort_flag)) break;
+                    rphase ^= 1;
+                    rpending = false;
+                    uint8_t* rowp = stage + lane * 128;
                     // x = x + (acc + bias), two columns per packed operation
                     const float4* bp = reinterpret_cast<const float4*>(args.bias + n);
                     float v[32];
 #pragma unroll
                     for (int q = 0; q < 8; ++q) {
+                        const float4 xq = *reinterpret_cast<const float4*>(rowp + ((q ^ (lane & 7)) << 4));
                         const float4 bb = args.bias ? __ldg(bp + q) : make_float4(0.f, 0.f, 0.f, 0.f);
                         const float2 s0 = __fadd2_rn(
                             make_float2(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1])),
@@ -732,36 +749,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfgT<BK>::THREAD
                         const float2 s1 = __fadd2_rn(
                             make_float2(__uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3])),
                             make_float2(bb.z, bb.w));
-                        const float2 t0 = __fadd2_rn(make_float2(xc[q].x, xc[q].y), s0);
-                        const float2 t1 = __fadd2_rn(make_float2(xc[q].z, xc[q].w), s1);
+                        const float2 t0 = __fadd2_rn(make_float2(xq.x, xq.y), s0);
+                        const float2 t1 = __fadd2_rn(make_float2(xq.z, xq.w), s1);
                         v[4 * q] = t0.x; v[4 * q + 1] = t0.y; v[4 * q + 2] = t1.x; v[4 * q + 3] = t1.y;
+                        *reinterpret_cast<float4*>(rowp + ((q ^ (lane & 7)) << 4)) = make_float4(t0.x, t0.y, t1.x, t1.y);
                     }
-                    if (lane == 0) bulk_wait_group_read<0>();   // the previous chunk's store has read the stage
-                    __syncwarp();
-                    uint8_t* rowp = stage + lane * 128;
-#pragma unroll
-                    for (int q = 0; q < 8; ++q)
-                        *reinterpret_cast<float4*>(rowp + ((q ^ (lane & 7)) << 4)) =
-                            make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
                     fence_proxy_async_smem();
                     __syncwarp();
                     if (lane == 0) {
-                        if (row0 < args.M) tma_store_2d(&tmC, stage, n, row0);
+                        tma_store_2d(&tmC, stage, n, row0);
                         bulk_commit_group();
+                        if (c + 1 < Cfg::WARP_COLS / 32) {
+                            bulk_wait_group_read<0>();   // the store has read the stage
+                            mbar_arrive_expect_tx(rload + (warp - 2), 32 * 32 * 4);
+                            tma_load_2d(stage, &tmC, rload + (warp - 2), n + 32, row0);
+                        }
                     }
-                    if (row_ok) {
-                        if (args.out_nchw) {
-                            const int img = m / kTokens, t = m - img * kTokens;
-                            float* o = args.out_nchw + (int64_t(img) * args.N + n) * kTokens + t;
+                    rpending = c + 1 < Cfg::WARP_COLS / 32;
+                    if (row_ok && args.out_nchw) {
+                        const int img = m / kTokens, t = m - img * kTokens;
+                        float* o = args.out_nchw + (int64_t(img) * args.N + n) * kTokens + t;
 #pragma unroll
-                            for (int i = 0; i < 32; ++i) o[int64_t(i) * kTokens] = v[i];
-                        }
-                        // the chunk two ahead reuses this register buffer
-                        if (c + 2 < Cfg::WARP_COLS / 32) {
-                            const float4* xr = reinterpret_cast<const float4*>(args.resid + int64_t(m) * args.N + n0);
-#pragma unroll
-                            for (int q = 0; q < 8; ++q) xc[q] = xr[(c + 2) * 8 + q];
-                        }
+                        for (int i = 0; i < 32; ++i) o[int64_t(i) * kTokens] = v[i];
                     }
                 }
             } else {
@@ -778,6 +787,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfgT<BK>::THREAD
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(tempty + acc), 0));
+        }
+        if constexpr (EPI == kEpiResid) {
+            // Gave up mid-tile: let the residual load in flight land before the CTA exits.
+            if (rpending) mbar_wait(rload + (warp - 2), rphase, args.status, kErrTimeoutDrain, nullptr);
         }
         if constexpr (Cfg::staged_out(EPI)) {
             if (lane == 0) bulk_wait_group_all();

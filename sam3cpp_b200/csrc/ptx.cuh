@@ -149,6 +149,13 @@ S3T_DEV void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t leader
         : "memory");
 }
 
+// Bring a tile of a tensor map into L2 (no shared-memory destination, no
+// completion to wait for).
+S3T_DEV void tma_prefetch_l2_2d(const CUtensorMap* map, int x, int y) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(map), "r"(x), "r"(y)
+                 : "memory");
+}
+
 // Make generic-proxy shared-memory writes visible to the async proxy (UMMA).
 // Tiled bulk store shared -> global (bulk-group completion).  Rows or
 // columns of the box outside the tensor are not written.
