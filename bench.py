@@ -43,6 +43,7 @@ METRIC = "ViT-trunk images/s @1008^2"
 FLOP_PER_IMAGE = 5.3986e12          # GEMMs 4609.6 GF + attention 782.8 GF + patch 6.24 GF
 GEMM_FLOP_PER_IMAGE_LAYER = 144.05e9  # 2*T*C*(3C + C + 2F), T=5184, C=1024, F=4736
 LAUNCHES_PER_TRUNK = 3 + 32 * 6 + 31  # im2col, patch GEMM, stem LN; 6 per block; 31 inter-block LNs
+GATHER_CHUNKS = 4                     # N > 1: pieces of a rank's shard whose gather overlaps the next piece
 # DRAM bytes (read + write) of the four GEMM launches of one block, per image:
 # one ncu capture of the four GEMM launches of block 0 of a 4-image trunk
 # (QKV 130 + proj 160 + fc1 197 + fc2 389 MB), scaled by the images a launch
@@ -163,13 +164,39 @@ def _run_ours(a, torch, dist, world, rank, local, dev):
     imgs_host = torch.from_numpy(syn.synthetic_images(per, start=rank * per)).pin_memory()
     imgs = imgs_host.to(dev)
     out = torch.empty((per, 1024, 72, 72), dtype=torch.float32, device=dev)
-    gathered = ([torch.empty_like(out) for _ in range(world)] if rank == 0 else None) if world > 1 else None
+    gathered = torch.empty((world, per, 1024, 72, 72), device=dev) if (rank == 0 and world > 1) else None
     stream = torch.cuda.current_stream(dev)
+    # N > 1: the shard runs in GATHER_CHUNKS pieces, and each piece's features
+    # go to rank 0 (NCCL point-to-point) while the next piece computes.
+    chunks = [(i * per // GATHER_CHUNKS, (i + 1) * per // GATHER_CHUNKS) for i in range(GATHER_CHUNKS)]
+    chunks = [c for c in chunks if c[1] > c[0]] if world > 1 else [(0, per)]
+    img_elems, out_elems = 3 * 1008 * 1008, 1024 * 72 * 72
 
-    def step():
-        trunk.run_device(imgs.data_ptr(), per, out.data_ptr(), stream.cuda_stream)
-        if world > 1:
-            dist.gather(out, gathered, dst=0)
+    def gather_piece(i0, i1):
+        if rank == 0:
+            ops = [dist.P2POp(dist.irecv, gathered[r, i0:i1], r) for r in range(1, world)]
+        else:
+            ops = [dist.P2POp(dist.isend, out[i0:i1], 0)]
+        return dist.batch_isend_irecv(ops)
+
+    def step(gather=True):
+        reqs = []
+        for i0, i1 in chunks:
+            trunk.run_device(imgs.data_ptr() + i0 * img_elems * 4, i1 - i0, out.data_ptr() + i0 * out_elems * 4,
+                             stream.cuda_stream)
+            if world > 1 and gather:
+                reqs += gather_piece(i0, i1)
+        for r in reqs:
+            r.wait()
+        if world > 1 and gather and rank == 0:
+            gathered[0].copy_(out, non_blocking=True)
+
+    def gather_only():
+        reqs = []
+        for i0, i1 in chunks:
+            reqs += gather_piece(i0, i1)
+        for r in reqs:
+            r.wait()
 
     def timed(fn, k):
         if world > 1:
@@ -196,6 +223,12 @@ def _run_ours(a, torch, dist, world, rank, local, dev):
     trunk.sync(stream.cuda_stream)
     ms_step = total_ms / a.steps
     value = a.images * a.steps / (total_ms / 1e3)
+    # the same step's parts on their own (not overlapped): trunk only, gather only
+    parts = {}
+    if world > 1:
+        k = max(1, min(a.steps, 5))
+        parts["trunk_only_ms_per_step"] = round(timed(lambda: step(gather=False), k) / k, 3)
+        parts["gather_only_ms_per_step"] = round(timed(gather_only, k) / k, 3)
 
     # e2e: public API with pinned host buffers (H2D + trunk + D2H per step)
     out_host = torch.empty((per, 1024, 72, 72), dtype=torch.float32).pin_memory()
@@ -216,6 +249,21 @@ def _run_ours(a, torch, dist, world, rank, local, dev):
     # per-kernel device time of the trunk's own launches at this shape: one
     # eager pass with a CUDA event after every launch, right after the timed region
     prof = trunk.profile(imgs.data_ptr(), per, out.data_ptr(), stream.cuda_stream)
+
+    # Q8_0 weights, same sharding and gather, fewer steps
+    q8 = {}
+    if a.format == "f16" and not a.no_extras:
+        qmodel = s3t.GgufModel(syn.synthetic_gguf("q8_0"), device=local)
+        trunk_f16, trunk = trunk, s3t.VisionTrunk(qmodel)
+        k = max(1, min(a.steps, 5))
+        step()
+        q8_ms = timed(step, k) / k
+        trunk.sync(stream.cuda_stream)
+        trunk = trunk_f16
+        q8 = {"q8_0": {"value": round(a.images / (q8_ms / 1e3), 3), "unit": "images/s", "ms_per_step": round(q8_ms, 3),
+                       "steps": k}}
+        qmodel.close()
+
     extras = {}
     if rank == 0 and world == 1 and not a.no_extras:
         extras = config_extras(torch, dev, stream, trunk, syn, s3t)
@@ -282,7 +330,9 @@ def _run_ours(a, torch, dist, world, rank, local, dev):
                 "d2h_bytes_per_step": int(out_host.numel() * 4 * world),
                 "wall_s": round(e2e_wall, 3)},
         "clocks": clk.summary(),
-        "gpu_launches": LAUNCHES_PER_TRUNK * a.steps * world,
+        "gpu_launches": LAUNCHES_PER_TRUNK * len(chunks) * a.steps * world,
+        **parts,
+        **q8,
         "attention": attn,
         "layernorm": norm,
         "trunk_profile_ms": {k: round(v[0], 3) for k, v in prof.items()},
@@ -475,21 +525,30 @@ def _cpu_model():
     return "unknown"
 
 
+def reference_build():
+    """The reference's CPU trunk as its CMake builds it by default
+    (GGML_NATIVE: -march=native; oracle/_ref/libsam3ref_native.so) when this
+    host has the build host's ISA extensions, else the AVX-512 / AVX2 build;
+    and the host's physical core count, the thread count it runs with."""
+    from oracle.pyoracle import Reference, physical_cores, reference_path
+    return Reference(reference_path(prefer_native=True)), physical_cores()
+
+
 def cpu_baseline(fmt):
     """The reference's own CPU trunk (oracle/_ref: ggml CPU backend compiled
-    from the reference sources) on one image with all host threads."""
+    from the reference sources) on one image, one thread per physical core,
+    and at its as-shipped 4 threads."""
     try:
-        from oracle.pyoracle import Reference
         from sam3cpp_b200 import synthetic as syn
-        ref = Reference()
-        threads = os.cpu_count() or 1
+        ref, threads = reference_build()
         path, img = syn.synthetic_gguf(fmt), syn.synthetic_image(0)
         _, sec = ref.trunk(path, img, threads)
         # also at the reference's as-shipped thread count (GGML_DEFAULT_N_THREADS = 4)
         _, sec4 = ref.trunk(path, img, 4)
         return {"value": round(1.0 / sec, 5), "unit": "images/s", "cores": threads, "kind": "reference",
                 "sample": f"1 image, sam3::VisionTrunk::run ({fmt.upper()} GGUF), {sec:.1f} s, "
-                          f"{ref.path.name}",
+                          f"{ref.path.name}, {threads} threads = physical cores "
+                          f"({os.cpu_count()} logical CPUs)",
                 "cpu_model": _cpu_model(),
                 "as_shipped_4_threads": {"value": round(1.0 / sec4, 5), "seconds": round(sec4, 2)}}
     except Exception as e:
@@ -503,10 +562,8 @@ def run_reference(a):
     world, rank, _ = dist_setup(a.gpus)
     if rank != 0:
         return
-    from oracle.pyoracle import Reference
     from sam3cpp_b200 import synthetic as syn
-    ref = Reference()
-    threads = os.cpu_count() or 1
+    ref, threads = reference_build()
     path = str(syn.synthetic_gguf(a.format))
     img = syn.synthetic_image(0)
     import ctypes as C
@@ -545,8 +602,8 @@ def run_reference(a):
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32 (ggml CPU)",
         "data": "synthetic (seeded random-init SAM 3 trunk weights, uniform[-1,1] images)",
         "config": {"workload": f"SAM 3 ViT trunk, {a.format.upper()} GGUF, 1 image per step (sample of the "
-                               f"{a.images}-image batch), ggml CPU backend, {threads} threads",
-                   "format": a.format},
+                               f"{a.images}-image batch), ggml CPU backend ({ref.path.name}), {threads} threads "
+                               f"= physical cores", "format": a.format},
         "cpu_baseline": {"value": round(value, 5), "unit": "images/s", "cores": threads, "kind": "reference",
                          "sample": f"{k} image(s) through sam3::VisionTrunk::run ({ref.path.name})"},
         "e2e": {"value": round(value, 5), "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},

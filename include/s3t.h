@@ -118,6 +118,35 @@ int s3t_trunk_profile(s3t_ctx *ctx, const float *images_dev, int batch, float *o
 /* Wait for the context's queued work and report any device-side error. */
 int s3t_sync(s3t_ctx *ctx, void *stream);
 
+/* --- several GPUs of one node -------------------------------------------
+ * No counterpart in the reference, which runs the trunk on one backend device
+ * (src/gguf_model.cpp:107-120).  The trunk is per image, so a batch is split
+ * into contiguous shards of ceil(batch / n_devices) images, one per GPU; each
+ * GPU holds its own copy of the weights and is driven by its own host thread.
+ * The only exchange is moving images in and feature maps out (peer copies,
+ * no collective inside the trunk).  A handle is not safe for concurrent calls. */
+typedef struct s3t_multi s3t_multi;
+
+/* Load the trunk of gguf_path onto every listed device (distinct device
+ * indices; devices[0] is the "first GPU" below).  NULL on error. */
+s3t_multi *s3t_multi_create(const int *devices, int n_devices, const char *gguf_path, const char *tensor_map_path);
+void s3t_multi_destroy(s3t_multi *m);
+int s3t_multi_num_devices(const s3t_multi *m);
+
+/* images [batch][3][1008][1008] -> out [batch][1024][72][72] fp32 NCHW.  Host
+ * buffers (flags 0): every GPU copies its own slices in and out; returns when
+ * the output is in host memory.  With S3T_IMAGES_ON_DEVICE /
+ * S3T_OUTPUT_ON_DEVICE the buffers are memory of devices[0]: the other GPUs
+ * peer-copy their images in and their features out (the gather to the first
+ * GPU), chunk by chunk so the copies overlap their compute.  `stream` is a
+ * stream of devices[0] (NULL: its context's own stream); with device buffers
+ * the call returns after enqueueing, and that stream waits for every GPU's
+ * work (check with s3t_multi_sync). */
+int s3t_multi_run(s3t_multi *m, const float *images_nchw, int batch, float *out_nchw, int flags, void *stream);
+
+/* Wait for every GPU's queued work of the handle and report device errors. */
+int s3t_multi_sync(s3t_multi *m, void *stream);
+
 /* --- op-level entry points (parity tests, microbenchmarks) --------------- */
 
 /* Dequantize GGUF weight bytes on the device to fp32: F16 and Q8_0

@@ -13,6 +13,7 @@ from __future__ import annotations
 import ctypes as C
 import json
 import os
+import re
 from pathlib import Path
 
 import numpy as np
@@ -260,15 +261,56 @@ def _cpu_flags() -> set[str]:
     return set()
 
 
-def reference_path() -> Path | None:
-    """Best oracle/_ref build for this host (v4 needs AVX-512 F/BW/DQ/VL)."""
+_ISA = re.compile(r"^(avx|amx|fma|f16c|bmi|sse|ssse|sha|vaes|vpclmul|gfni|movbe|popcnt|abm|adx|aes|pclmul|movdir|"
+                  r"serialize|waitpkg|cldemote|clwb|clflushopt|rdpid|rdseed|rdrand|xsave)")
+
+
+def native_build_usable(flags: set[str] | None = None) -> bool:
+    """The -march=native build runs here only if this host has every ISA
+    extension the build host had (recorded next to the library)."""
+    rec = HERE / "_ref" / "libsam3ref_native.flags"
+    if not rec.exists() or not (HERE / "_ref" / "libsam3ref_native.so").exists():
+        return False
+    need = {f for f in rec.read_text().split() if _ISA.match(f)}
+    return need <= (flags if flags is not None else _cpu_flags())
+
+
+def reference_path(prefer_native: bool = False) -> Path | None:
+    """oracle/_ref build for this host: v4 (AVX-512 F/BW/DQ/VL) or v3; with
+    prefer_native, the -march=native build when this host can run it (the
+    reference's default GGML_NATIVE build, used for the timed CPU baseline).
+    The golden fixtures were made with v4, so the checkers use v4."""
     flags = _cpu_flags()
+    if prefer_native and native_build_usable(flags):
+        return HERE / "_ref" / "libsam3ref_native.so"
     v4 = {"avx512f", "avx512bw", "avx512dq", "avx512vl"} <= flags
     for name in (["libsam3ref_v4.so"] if v4 else []) + ["libsam3ref_v3.so"]:
         p = HERE / "_ref" / name
         if p.exists():
             return p
     return None
+
+
+def physical_cores() -> int:
+    """Distinct (physical id, core id) pairs of /proc/cpuinfo: the host's
+    physical cores (hyperthreads counted once)."""
+    cores, phys, core = set(), "0", None
+    try:
+        for line in open("/proc/cpuinfo"):
+            k, _, v = line.partition(":")
+            k, v = k.strip(), v.strip()
+            if k == "physical id":
+                phys = v
+            elif k == "core id":
+                core = v
+            elif not k and core is not None:
+                cores.add((phys, core))
+                core = None
+        if core is not None:
+            cores.add((phys, core))
+    except OSError:
+        pass
+    return len(cores) or (os.cpu_count() or 1)
 
 
 class Reference:

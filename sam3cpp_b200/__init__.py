@@ -23,7 +23,7 @@ from typing import Sequence
 
 import numpy as np
 
-__all__ = ["GgufModel", "VisionTrunk", "VisionTrunkOutput", "lib", "S3TError",
+__all__ = ["GgufModel", "VisionTrunk", "VisionTrunkOutput", "MultiTrunk", "lib", "S3TError",
            "IMAGES_ON_DEVICE", "OUTPUT_ON_DEVICE"]
 
 _PKG = Path(__file__).resolve().parent
@@ -73,6 +73,12 @@ def lib() -> C.CDLL:
         L.s3t_trunk_profile.argtypes = [p, p, i, p, p, C.POINTER(C.c_double), C.POINTER(C.c_int)]
         L.s3t_selftest_wait_timeout.argtypes = [i, i]
         L.s3t_mha_d32.argtypes = [i, p, p, p, i, i, i, p, p, i, p]
+        L.s3t_multi_create.argtypes = [C.POINTER(i), i, C.c_char_p, C.c_char_p]
+        L.s3t_multi_create.restype = p
+        L.s3t_multi_destroy.argtypes = [p]
+        L.s3t_multi_num_devices.argtypes = [p]
+        L.s3t_multi_run.argtypes = [p, p, i, p, i, p]
+        L.s3t_multi_sync.argtypes = [p, p]
         _lib = L
     return _lib
 
@@ -237,6 +243,59 @@ class VisionTrunk:
 
     def sync(self, stream: int = 0) -> None:
         check(lib().s3t_sync(self.model.ctx, C.c_void_p(stream) if stream else None))
+
+
+class MultiTrunk:
+    """The trunk on several GPUs of one node (s3t_multi_*): one weight replica
+    and one host thread per GPU, images sharded by image (ceil(B / n) per
+    GPU), feature maps gathered to the first GPU by peer copies (device
+    buffers) or copied straight to the caller's host buffer (host buffers).
+    The reference has no multi-GPU path (src/gguf_model.cpp:107-120 picks one
+    device)."""
+
+    def __init__(self, path: str | Path, devices: Sequence[int], tensor_map_path: str | None = None):
+        L = lib()
+        devs = (C.c_int * len(devices))(*devices)
+        self._h = L.s3t_multi_create(devs, len(devices), str(path).encode(),
+                                     tensor_map_path.encode() if tensor_map_path else None)
+        if not self._h:
+            raise S3TError(L.s3t_last_error().decode())
+        self.devices = list(devices)
+
+    @property
+    def n_devices(self) -> int:
+        return lib().s3t_multi_num_devices(self._h)
+
+    def run_batch(self, images: np.ndarray) -> np.ndarray:
+        """images [B,3,1008,1008] fp32 (host) -> [B,1024,72,72] fp32 (host)."""
+        images = np.ascontiguousarray(images, dtype=np.float32)
+        if images.ndim != 4 or images.shape[1:] != (3, IMAGE, IMAGE):
+            raise S3TError("vision trunk expects NCHW images [B, 3, 1008, 1008]")
+        out = np.empty((images.shape[0], DIM, GRID, GRID), np.float32)
+        check(lib().s3t_multi_run(self._h, images.ctypes.data, images.shape[0], out.ctypes.data, 0, None))
+        return out
+
+    def run_device(self, images_ptr: int, batch: int, out_ptr: int, stream: int = 0, images_on_device: bool = True,
+                   output_on_device: bool = True) -> None:
+        """Raw-pointer form; device pointers are memory of the first GPU and
+        `stream` a stream of it (enqueued, see sync)."""
+        flags = (IMAGES_ON_DEVICE if images_on_device else 0) | (OUTPUT_ON_DEVICE if output_on_device else 0)
+        check(lib().s3t_multi_run(self._h, C.c_void_p(images_ptr), batch, C.c_void_p(out_ptr), flags,
+                                  C.c_void_p(stream) if stream else None))
+
+    def sync(self, stream: int = 0) -> None:
+        check(lib().s3t_multi_sync(self._h, C.c_void_p(stream) if stream else None))
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().s3t_multi_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 MHA_BF16 = 1

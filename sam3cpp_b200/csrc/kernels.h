@@ -158,6 +158,8 @@ bool make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, in
 struct s3t_ctx;
 namespace s3t {
 bool ctx_stem_view(const s3t_ctx* ctx, StemView* out);
+// The context's own stream (what a NULL stream argument means), or null.
+cudaStream_t ctx_stream(const s3t_ctx* ctx);
 // Records the thread-local message returned by s3t_last_error(); returns -1.
 int set_last_error(const char* msg);
 }  // namespace s3t

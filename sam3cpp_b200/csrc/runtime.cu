@@ -417,7 +417,7 @@ int dev_alloc(std::vector<void*>& list, T** p, size_t bytes) {
     return 0;
 }
 
-constexpr size_t kMaxGraphs = 8;
+constexpr size_t kMaxGraphs = 16;
 
 void free_graphs(s3t_ctx* c) {
     for (auto& kv : c->graphs) cudaGraphExecDestroy(kv.second.exec);
@@ -743,6 +743,8 @@ int upload_f32_vec(s3t_ctx* c, const Staged& s, int64_t n, float** dst) {
 }  // namespace
 
 int s3t::set_last_error(const char* msg) { return fail(msg); }
+
+cudaStream_t s3t::ctx_stream(const s3t_ctx* c) { return c ? c->stream : nullptr; }
 
 bool s3t::ctx_stem_view(const s3t_ctx* c, StemView* out) {
     if (!c || !c->finalized || !out) return false;

@@ -62,3 +62,10 @@ def test_python_mirror_raises_without_gpu(libs3t):
     import sam3cpp_b200 as s3t
     with pytest.raises(s3t.S3TError):
         s3t.GgufModel("/nonexistent.gguf")
+
+
+def test_multi_gpu_handle_fails_cleanly_without_arguments(libs3t):
+    assert not libs3t.s3t_multi_create(None, 0, b"x.gguf", None)
+    assert b"devices" in libs3t.s3t_last_error()
+    assert libs3t.s3t_multi_run(None, None, 1, None, 0, None) == -1
+    assert libs3t.s3t_multi_num_devices(None) == 0

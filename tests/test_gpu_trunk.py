@@ -174,14 +174,14 @@ def test_trunk_profile_pass(gpu, torch_cuda):
 
 def test_graph_cache_eviction(gpu, torch_cuda):
     """A caller that hands the trunk a fresh output buffer on every call makes
-    the context capture a graph per (input, output) pair; beyond 8 the least
+    the context capture a graph per (input, output) pair; beyond 16 the least
     recently used graph is dropped, and every run still computes the same."""
     from sam3cpp_b200 import synthetic as s
     torch = torch_cuda
     path, _ = _models("f16", 2, True)
     trunk = gpu.VisionTrunk(gpu.GgufModel(path))
     img = torch.from_numpy(s.synthetic_images(1)).cuda()
-    outs = [torch.empty((1, 1024, 72, 72), device="cuda") for _ in range(11)]
+    outs = [torch.empty((1, 1024, 72, 72), device="cuda") for _ in range(19)]
     for o in outs + outs[:3]:
         trunk.run_device(img.data_ptr(), 1, o.data_ptr())
     trunk.sync()
