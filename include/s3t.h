@@ -197,7 +197,15 @@ int s3t_attention(int device, const void *q, const void *k, const void *v, int g
  * 201 queries (:430, no mask) and the text cross attention with the prompt
  * mask row (:443).  The decoder computes softmax explicitly (ggml_soft_max_ext):
  * the result is the same, except that a row with every key at -inf is NaN
- * there and 0 here. */
+ * there and 0 here.
+ * Scratch: when the query tiles cannot fill the GPU and there are 16 or more
+ * blocks of 64 keys (the decoder's 201 queries against 5184 image tokens),
+ * each tile's keys are split into ranges computed in parallel and merged;
+ * the call then allocates a stream-ordered scratch buffer of about
+ * batch * ceil(q_len / 128) * 128 * 8 heads * splits * 34 floats
+ * (cudaMallocAsync on `stream`, freed with cudaFreeAsync on the same stream;
+ * 5.3 MB for that decoder call, split 19 ways).  Every other call allocates
+ * nothing. */
 #define S3T_MHA_BIAS 4
 int s3t_mha_d32(int device, const void *q_dev, const void *k_dev, const void *v_dev, int batch, int q_len,
                 int kv_len, const float *key_mask_dev, void *out_dev, int flags, void *stream);

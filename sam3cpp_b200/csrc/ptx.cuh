@@ -378,26 +378,6 @@ S3T_DEV float rcp_approx(float x) {
     return y;
 }
 
-// 2^x for x <= 0 on the FMA/ALU pipes, used for a share of the softmax
-// exponentials so the SFU is not the only unit doing them (the split used
-// by FlashAttention-4).  Range reduction x = n + f, n = round(x), f in
-// [-1/2, 1/2]; 2^f by a degree-4 polynomial whose coefficients are this
-// project's own minimax fit of relative error on that interval (max 2.7e-6
-// in fp32); 2^n applied by adding n to the exponent field.
-S3T_DEV float exp2_poly(float x) {
-    x = fmaxf(x, -125.0f);
-    const float magic = 12582912.0f;  // 1.5 * 2^23: x + magic rounds x to an integer
-    const float t = x + magic;
-    const float n = t - magic;
-    const float f = x - n;
-    float p = fmaf(9.569674936e-03f, f, 5.591824792e-02f);
-    p = fmaf(p, f, 2.402476669e-01f);
-    p = fmaf(p, f, 6.931217338e-01f);
-    p = fmaf(p, f, 9.999992361e-01f);
-    const int ni = __float_as_int(t) - __float_as_int(magic);
-    return __int_as_float(__float_as_int(p) + (ni << 23));
-}
-
 // GELU with the error function of Abramowitz & Stegun, Handbook of
 // Mathematical Functions, formula 7.1.26 (|erf error| <= 1.5e-7):
 // erf(z) = 1 - (a1 t + ... + a5 t^5) exp(-z^2), t = 1/(1 + p z), z >= 0.

@@ -166,7 +166,11 @@ def write_gguf(path: str | os.PathLike, weights: dict[str, np.ndarray], fmt: str
 
 
 def cache_dir() -> Path:
-    d = Path(os.environ.get("S3T_CACHE", "/tmp/s3t_synth"))
+    """Where seeded files are cached: $S3T_CACHE, else s3t_synth in the
+    system's temporary directory (outside the source tree: the full-size
+    files are 0.5-1.8 GB)."""
+    import tempfile
+    d = Path(os.environ.get("S3T_CACHE") or Path(tempfile.gettempdir()) / "s3t_synth")
     d.mkdir(parents=True, exist_ok=True)
     return d
 
