@@ -344,6 +344,9 @@ class Reference:
         if hasattr(L, "ref_trunk_block"):
             L.ref_trunk_stem.argtypes = [_p, _p, _p]
             L.ref_trunk_block.argtypes = [_p, C.c_int, _p, _p]
+        if hasattr(L, "ref_neck_first"):
+            L.ref_neck_first.argtypes = [_p, C.c_int, _p, _p, C.POINTER(C.c_int64)]
+            L.ref_neck_run.argtypes = [_p, C.c_int, _p, _p, C.POINTER(C.c_int64)]
 
     def _check(self, rc):
         if rc != 0:
@@ -474,6 +477,22 @@ class RefModel:
         out = np.empty_like(x)
         self.ref._check(self.ref.lib.ref_trunk_block(self.h, layer, _ptr(x), _ptr(out)))
         return out
+
+    def _neck(self, fn, level: int, trunk_nchw) -> np.ndarray:
+        x = np.ascontiguousarray(trunk_nchw, np.float32).reshape(1, 1024, 72, 72)
+        out = np.empty(256 * 288 * 288, np.float32)       # the largest output (level 0: 4 x 4 upsampled)
+        shape = (C.c_int64 * 4)()
+        self.ref._check(fn(self.h, level, _ptr(x), _ptr(out), shape))
+        n = int(np.prod(list(shape)))
+        return out[:n].reshape(tuple(shape))
+
+    def neck_first(self, level: int, trunk_nchw) -> np.ndarray:
+        """The first operation of neck level `level` as a ggml graph (ref_neck_first)."""
+        return self._neck(self.ref.lib.ref_neck_first, level, trunk_nchw)
+
+    def neck_run(self, level: int, trunk_nchw) -> np.ndarray:
+        """sam3::VisionNeck::run for one level (ref_neck_run)."""
+        return self._neck(self.ref.lib.ref_neck_run, level, trunk_nchw)
 
     def close(self):
         if self.h:

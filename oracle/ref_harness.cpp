@@ -15,12 +15,14 @@
 #include "ggml-backend.h"
 #include "sam3/gguf_model.h"
 #include "sam3/vision_trunk.h"
+#include "sam3/vision_neck.h"
 
 #include <chrono>
 #include <cmath>
 #include <cstdint>
 #include <cstring>
 #include <exception>
+#include <optional>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -492,6 +494,97 @@ int ref_trunk_block(void * handle, int layer, const float * x, float * out) {
         ffn = ggml_gelu_erf(ctx, ffn);
         ffn = dense(ctx, need(m, b + ".mlp.fc2.weight"), need(m, b + ".mlp.fc2.bias"), ffn);
         g.run(ggml_add(ctx, cur, ffn), out);
+        return 0;
+    } catch (const std::exception & e) {
+        g_err = e.what();
+        return -1;
+    }
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// The vision neck (src/vision_neck.cpp), the consumer of the trunk's output.
+
+extern "C" {
+
+// sam3::VisionNeck::run (src/vision_neck.cpp:203-393) for one level
+// (only_level) of the model behind `handle`: trunk [1][1024][72][72] fp32 NCHW
+// -> out, the level's NCHW feature map.  shape[4] receives its shape.
+int ref_neck_run(void * handle, int level, const float * trunk, float * out, int64_t * shape) {
+    try {
+        const auto & m = *static_cast<const sam3::GgufModel *>(handle);
+        std::vector<float> x(trunk, trunk + size_t(kC) * kG * kG);
+        sam3::VisionNeck neck(m);
+        const sam3::VisionNeckOutput r = neck.run(x, {1, kC, kG, kG}, std::optional<int>(level));
+        std::memcpy(out, r.levels[0].data(), r.levels[0].size() * sizeof(float));
+        for (int i = 0; i < 4; ++i) shape[i] = r.shapes[0][i];
+        return 0;
+    } catch (const std::exception & e) {
+        g_err = e.what();
+        return -1;
+    }
+}
+
+}  // extern "C"
+
+namespace {
+
+ggml_tensor * conv_bias(ggml_context * ctx, ggml_tensor * w, ggml_tensor * b, ggml_tensor * x) {
+    // MLX [OC, KH, KW, IC] lands in ggml as ne [IC, KW, KH, OC]; ggml_conv_2d
+    // takes [KW, KH, IC, OC].  1x1, stride 1, no padding.
+    ggml_tensor * wk = ggml_cont(ctx, ggml_permute(ctx, w, 2, 0, 1, 3));
+    ggml_tensor * y = ggml_conv_2d(ctx, wk, x, 1, 1, 0, 0, 1, 1);
+    ggml_tensor * bb = ggml_reshape_4d(ctx, f32(ctx, b), 1, 1, wk->ne[3], 1);
+    return ggml_add(ctx, y, bb);
+}
+
+// 2x2 stride-2 transposed conv as one mul_mat over the channels plus a pixel
+// shuffle, on x [W, H, IC, 1] -> [W*2, H*2, OC, 1] (NCHW order).
+ggml_tensor * deconv_bias(ggml_context * ctx, ggml_tensor * w, ggml_tensor * b, ggml_tensor * x) {
+    const int64_t ic = w->ne[0], oc = w->ne[3], wd = x->ne[0], ht = x->ne[1];
+    ggml_tensor * wf = ggml_reshape_2d(ctx, ggml_cont(ctx, ggml_permute(ctx, w, 0, 2, 3, 1)), ic, oc * 4);
+    ggml_tensor * xf = ggml_reshape_2d(ctx, ggml_cont(ctx, ggml_permute(ctx, x, 2, 0, 1, 3)), ic, wd * ht);
+    ggml_tensor * y = ggml_mul_mat(ctx, wf, xf);                                  // [oc*4, W*H], row oc + oc*(kw + 2 kh)
+    y = ggml_reshape_4d(ctx, y, oc * 2, 2, wd, ht);                               // [oc, kw | kh | W | H]
+    y = ggml_cont(ctx, ggml_permute(ctx, y, 0, 2, 1, 3));                         // [oc*2, W, kh, H]
+    y = ggml_reshape_4d(ctx, y, oc, 2 * wd, 2 * ht, 1);                           // [oc, 2W, 2H]
+    y = ggml_add(ctx, y, ggml_reshape_4d(ctx, f32(ctx, b), oc, 1, 1, 1));
+    return ggml_cont(ctx, ggml_permute(ctx, y, 2, 0, 1, 3));                      // [2W, 2H, oc]
+}
+
+}  // namespace
+
+extern "C" {
+
+// The first operation of neck level `level` (src/vision_neck.cpp:262-345) on
+// trunk [1][1024][72][72] fp32 NCHW, as its own ggml graph: level 0 the first
+// 2x2 deconv + bias followed by its GELU, level 1 the 2x2 deconv + bias,
+// level 2 the 1x1 conv + bias, level 3 the 2x2 max pool then the 1x1 conv +
+// bias.  out receives the NCHW result, shape[4] its shape.
+int ref_neck_first(void * handle, int level, const float * trunk, float * out, int64_t * shape) {
+    try {
+        const auto & m = *static_cast<const sam3::GgufModel *>(handle);
+        const std::string p = "backbone.vision_backbone.convs." + std::to_string(level) + ".";
+        OneGraph g(m);
+        ggml_context * ctx = g.ctx;
+        ggml_tensor * x = g.input(GGML_TYPE_F32, kG, kG, kC, 1, trunk);
+        ggml_tensor * y = nullptr;
+        if (level == 0) {
+            y = ggml_gelu_erf(ctx, deconv_bias(ctx, need(m, p + "dconv_2x2_0.weight"), need(m, p + "dconv_2x2_0.bias"), x));
+        } else if (level == 1) {
+            y = deconv_bias(ctx, need(m, p + "dconv_2x2.weight"), need(m, p + "dconv_2x2.bias"), x);
+        } else if (level == 2 || level == 3) {
+            if (level == 3) x = ggml_pool_2d(ctx, x, GGML_OP_POOL_MAX, 2, 2, 2, 2, 0, 0);
+            y = conv_bias(ctx, need(m, p + "conv_1x1.weight"), need(m, p + "conv_1x1.bias"), x);
+        } else {
+            throw std::runtime_error("level must be in [0, 3]");
+        }
+        g.run(y, out);
+        shape[0] = 1;
+        shape[1] = y->ne[2];
+        shape[2] = y->ne[1];
+        shape[3] = y->ne[0];
         return 0;
     } catch (const std::exception & e) {
         g_err = e.what();

@@ -92,6 +92,38 @@ def make_f32_weights(seed: int = 0, layers: int = LAYERS, perturb: bool = False)
     return w
 
 
+NECK = "backbone.vision_backbone.convs"
+# The SAM 3 neck (src/vision_neck.cpp:262-347): output channels of each conv
+# and, per level, the layers in order.  MLX layouts: Conv2d and
+# ConvTranspose2d weights [OC, KH, KW, IC].
+NECK_LAYERS = {
+    0: [("dconv_2x2_0", 512, 2, DIM), ("dconv_2x2_1", 256, 2, 512), ("conv_1x1", 256, 1, 256), ("conv_3x3", 256, 3, 256)],
+    1: [("dconv_2x2", 512, 2, DIM), ("conv_1x1", 256, 1, 512), ("conv_3x3", 256, 3, 256)],
+    2: [("conv_1x1", 256, 1, DIM), ("conv_3x3", 256, 3, 256)],
+    3: [("conv_1x1", 256, 1, DIM), ("conv_3x3", 256, 3, 256)],
+}
+
+
+def make_neck_weights(seed: int = 0, identity_3x3: bool = False) -> dict[str, np.ndarray]:
+    """Seeded neck weights (default_rng(seed + 104729), drawn level by level in
+    NECK_LAYERS order): conv/deconv weights N(0, 0.02), biases N(0, 0.1).
+    identity_3x3 replaces every conv_3x3 by the identity (centre tap 1 on the
+    diagonal, bias 0), so a level's output equals its 1x1 conv's output."""
+    rng = np.random.default_rng(seed + 104729)
+    w: dict[str, np.ndarray] = {}
+    for lvl, layers in NECK_LAYERS.items():
+        for name, oc, k, ic in layers:
+            key = f"{NECK}.{lvl}.{name}"
+            wt = rng.standard_normal((oc, k, k, ic), dtype=np.float32) * np.float32(0.02)
+            b = rng.standard_normal(oc, dtype=np.float32) * np.float32(0.1)
+            if identity_3x3 and name == "conv_3x3":
+                wt = np.zeros((oc, k, k, ic), np.float32)
+                wt[np.arange(oc), 1, 1, np.arange(oc)] = 1.0
+                b = np.zeros(oc, np.float32)
+            w[key + ".weight"], w[key + ".bias"] = wt, b
+    return w
+
+
 def is_sensitive(name: str) -> bool:
     """convert_mlx_sam3_to_gguf.py:223-229 (bias, *norm*, pos_embed stay F32)."""
     low = name.lower()
@@ -175,12 +207,18 @@ def cache_dir() -> Path:
     return d
 
 
-def synthetic_gguf(fmt: str, seed: int = 0, layers: int = LAYERS, perturb: bool = False) -> Path:
-    """Path of the cached seeded GGUF for ``fmt`` (created on first use)."""
-    tag = f"sam3_trunk_{fmt}_s{seed}_L{layers}{'_p' if perturb else ''}.gguf"
+def synthetic_gguf(fmt: str, seed: int = 0, layers: int = LAYERS, perturb: bool = False, neck: bool = False,
+                   identity_3x3: bool = False) -> Path:
+    """Path of the cached seeded GGUF for ``fmt`` (created on first use);
+    neck=True appends the seeded neck weights (make_neck_weights)."""
+    tag = (f"sam3_trunk_{fmt}_s{seed}_L{layers}{'_p' if perturb else ''}"
+           f"{('_neck' + ('_id3' if identity_3x3 else '')) if neck else ''}.gguf")
     p = cache_dir() / tag
     if not p.exists():
-        write_gguf(p, make_f32_weights(seed, layers, perturb), fmt)
+        w = make_f32_weights(seed, layers, perturb)
+        if neck:
+            w.update(make_neck_weights(seed, identity_3x3))
+        write_gguf(p, w, fmt)
     return p
 
 
