@@ -118,6 +118,32 @@ int s3t_trunk_profile(s3t_ctx *ctx, const float *images_dev, int batch, float *o
 /* Wait for the context's queued work and report any device-side error. */
 int s3t_sync(s3t_ctx *ctx, void *stream);
 
+/* --- the vision neck's first operation, on the trunk's device output -------
+ * The reference hands the trunk's output to sam3::VisionNeck::run as a host
+ * vector (src/pipeline.cpp:159-163, src/vision_neck.cpp:203-206), a full D2H
+ * and H2D in between.  These take the trunk's NCHW output where
+ * s3t_trunk_run (S3T_OUTPUT_ON_DEVICE) left it and run the first operation of
+ * one neck level (src/vision_neck.cpp:262-345) with the neck weights the same
+ * GGUF file holds (backbone.vision_backbone.convs.*):
+ *   level 0: 2x2 stride-2 transposed conv dconv_2x2_0 + bias, then GELU
+ *            (the input of the second transposed conv) -> [B][512][144][144]
+ *   level 1: 2x2 stride-2 transposed conv dconv_2x2 + bias -> [B][512][144][144]
+ *   level 2: 1x1 conv conv_1x1 + bias                      -> [B][256][72][72]
+ *   level 3: 2x2 max pool, then 1x1 conv conv_1x1 + bias   -> [B][256][36][36]
+ * (channel counts as the file gives them; s3t_neck_first_shape reports them).
+ * trunk_dev [batch][1024][72][72] and out_dev are fp32 device memory of the
+ * context's GPU; enqueued on `stream` (NULL: the context's own stream).  The
+ * operands are fp16 with fp32 accumulation and the result passes through
+ * fp16.  The transposed conv multiplies the values in the order the
+ * reference's graph reads them (its ggml_permute(x, 2, 0, 1, 3) on [W, H, C],
+ * :96-105).  Uses the context's workspace: not concurrently with a trunk run
+ * on the same context. */
+int s3t_neck_first(s3t_ctx *ctx, int level, const float *trunk_dev, int batch, float *out_dev, void *stream);
+
+/* Shape [1][C][H][W] of s3t_neck_first's output for one image, or -1 if the
+ * file holds no weights for that level. */
+int s3t_neck_first_shape(const s3t_ctx *ctx, int level, int64_t shape[4]);
+
 /* --- several GPUs of one node -------------------------------------------
  * No counterpart in the reference, which runs the trunk on one backend device
  * (src/gguf_model.cpp:107-120).  The trunk is per image, so a batch is split

@@ -73,6 +73,8 @@ def lib() -> C.CDLL:
         L.s3t_trunk_profile.argtypes = [p, p, i, p, p, C.POINTER(C.c_double), C.POINTER(C.c_int)]
         L.s3t_selftest_wait_timeout.argtypes = [i, i]
         L.s3t_mha_d32.argtypes = [i, p, p, p, i, i, i, p, p, i, p]
+        L.s3t_neck_first.argtypes = [p, i, p, i, p, p]
+        L.s3t_neck_first_shape.argtypes = [p, i, C.POINTER(i64)]
         L.s3t_multi_create.argtypes = [C.POINTER(i), i, C.c_char_p, C.c_char_p]
         L.s3t_multi_create.restype = p
         L.s3t_multi_destroy.argtypes = [p]
@@ -229,6 +231,18 @@ class VisionTrunk:
         flags = (IMAGES_ON_DEVICE if images_on_device else 0) | (OUTPUT_ON_DEVICE if output_on_device else 0)
         check(lib().s3t_trunk_run(self.model.ctx, C.c_void_p(images_ptr), batch, C.c_void_p(out_ptr), flags,
                                   C.c_void_p(stream) if stream else None))
+
+    def neck_first_shape(self, level: int) -> tuple[int, int, int, int]:
+        """[1, C, H, W] of the neck level's first-operation output (one image)."""
+        shape = (C.c_int64 * 4)()
+        check(lib().s3t_neck_first_shape(self.model.ctx, level, shape))
+        return tuple(shape)
+
+    def neck_first_device(self, level: int, trunk_ptr: int, batch: int, out_ptr: int, stream: int = 0) -> None:
+        """The first operation of neck level `level` on the trunk's device NCHW
+        output (s3t_neck_first); enqueued on `stream`."""
+        check(lib().s3t_neck_first(self.model.ctx, level, C.c_void_p(trunk_ptr), batch, C.c_void_p(out_ptr),
+                                   C.c_void_p(stream) if stream else None))
 
     PROFILE_KINDS = ("stem", "qkv", "attn_windowed", "attn_global", "proj", "layernorm", "fc1", "fc2")
 

@@ -106,6 +106,14 @@ cudaError_t launch_rope_inplace(void* x, int groups, int L, int windowed, int bf
 cudaError_t gemm_prepare();
 cudaError_t attention_prepare();
 
+// The neck's first operation around the pair GEMM (s3t_neck_first): the
+// trunk's NCHW fp32 output [batch][1024][72][72] -> the fp16 A operand
+// (levels 0/1: the 2x2 deconv's input order; 2: tokens; 3: 2x2 max-pooled
+// tokens), and the GEMM's fp16 [batch*T][rows] -> the level's NCHW fp32 map.
+cudaError_t launch_neck_tokens(const float* x, int batch, int level, __half* a, cudaStream_t stream);
+cudaError_t launch_neck_out(const __half* y, int batch, int level, int oc, float* out, cudaStream_t stream);
+cudaError_t neck_prepare();
+
 // Multi-head attention of the encoder fusion (src/encoder_fusion.cpp:63-88):
 // 8 heads of 32 over token-major [len][256] q/k/v, ggml_flash_attn_ext
 // semantics with an optional additive per-key mask; `batch` independent

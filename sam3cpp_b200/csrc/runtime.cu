@@ -46,6 +46,7 @@ int fail(const std::string& msg) {
     } while (0)
 
 const char* kPrefix = "backbone.vision_backbone.trunk";
+const char* kNeckPrefix = "backbone.vision_backbone.convs.";   // the neck (src/vision_neck.cpp)
 
 bool is_global_attention_block(int layer) {  // src/vision_trunk.cpp:46-48
     return layer == 7 || layer == 15 || layer == 23 || layer == 31;
@@ -106,6 +107,7 @@ int device_state(int device, DeviceState** out) {
         S3T_CUDA(gemm_prepare());
         S3T_CUDA(attention_prepare());
         S3T_CUDA(mha32_prepare());
+        S3T_CUDA(neck_prepare());
         const std::vector<float> rl = rope_table(1.0f, kWindow);
         const std::vector<float> rg = rope_table(float(kWindow) / float(kGrid), kGrid);
         S3T_CUDA(cudaMalloc(&d.rope_local, rl.size() * 4));
@@ -324,7 +326,7 @@ int open_gguf(const char* path, const char* map_path, GgufFile& f) {
     for (const auto& t : ts) {
         auto al = s2o.find(t.name);
         const std::string& orig = al != s2o.end() ? al->second : t.name;
-        if (orig.rfind(kPrefix, 0) != 0) continue;
+        if (orig.rfind(kPrefix, 0) != 0 && orig.rfind(kNeckPrefix, 0) != 0) continue;
         int64_t n = 1;
         for (int d = 0; d < 4; ++d) {
             if (t.ne[d] <= 0 || t.ne[d] > (int64_t(1) << 40) / n) return fail("corrupt GGUF shape for " + orig);
@@ -380,6 +382,14 @@ struct s3t_ctx {
     float* pos = nullptr;
     float *lnpre_w = nullptr, *lnpre_b = nullptr;
     LayerW layers[kLayers];
+    // The first operation of each neck level (s3t_neck_first), when the file
+    // holds the neck: fp16 weight rows [rows][1024] and fp32 bias per row.
+    struct NeckFirst {
+        int oc = 0, rows = 0;     // output channels; GEMM rows (4 * oc for a 2x2 deconv)
+        __half* w = nullptr;
+        float* bias = nullptr;
+        std::string missing;      // why the level is unavailable
+    } neck[4];
 
     int ws_batch = 0;
     std::vector<void*> ws_allocs;
@@ -740,6 +750,63 @@ int upload_f32_vec(s3t_ctx* c, const Staged& s, int64_t n, float** dst) {
     return 0;
 }
 
+// The neck's first operations as GEMM weight rows (src/vision_neck.cpp:262-345):
+// level 0 convs.0.dconv_2x2_0 and level 1 convs.1.dconv_2x2 (2x2 stride-2
+// transposed convs, ggml ne [IC, KW, KH, OC]: row r = oc + OC * (kw + 2 kh), the
+// row order of deconv2d_bias's mul_mat, :91-93); levels 2 and 3 convs.N.conv_1x1
+// (ne [IC, 1, 1, OC]: row = oc).  F16 values are kept, F32 ones rounded to fp16.
+// A level whose tensors the file does not hold is left unavailable.
+int prepare_neck(s3t_ctx* c) {
+    const std::string P(kNeckPrefix);
+    const char* names[4] = {"0.dconv_2x2_0", "1.dconv_2x2", "2.conv_1x1", "3.conv_1x1"};
+    for (int lvl = 0; lvl < 4; ++lvl) {
+        auto& nf = c->neck[lvl];
+        const std::string wn = P + names[lvl] + ".weight", bn = P + names[lvl] + ".bias";
+        auto wi = c->staged.find(wn), bi = c->staged.find(bn);
+        if (wi == c->staged.end() || bi == c->staged.end()) {
+            nf.missing = "missing tensor: " + (wi == c->staged.end() ? wn : bn);
+            continue;
+        }
+        const Staged& ws = wi->second;
+        const Staged& bs = bi->second;
+        const int k = lvl < 2 ? 2 : 1;
+        const int64_t oc = ws.ne[3];
+        if (ws.ne[0] != kDim || ws.ne[1] != k || ws.ne[2] != k || oc <= 0 || oc % 32 || oc > kMlp / 4 ||
+            bs.ne[0] != oc || bs.ne[1] * bs.ne[2] * bs.ne[3] != 1)
+            return fail("unexpected shape for " + wn);
+        if ((ws.type != S3T_TYPE_F16 && ws.type != S3T_TYPE_F32) || (bs.type != S3T_TYPE_F32 && bs.type != S3T_TYPE_F16))
+            return fail("unsupported type for " + wn);
+        const int rows = int(oc) * k * k;
+        std::vector<__half> wr(size_t(rows) * kDim);
+        std::vector<float> br(rows);
+        auto wval = [&](size_t i) -> float {
+            if (ws.type == S3T_TYPE_F32) {
+                float v;
+                memcpy(&v, ws.host.data() + i * 4, 4);
+                return v;
+            }
+            return __half2float(reinterpret_cast<const __half*>(ws.host.data())[i]);
+        };
+        for (int o = 0; o < oc; ++o) {
+            const float bv = bs.type == S3T_TYPE_F32 ? reinterpret_cast<const float*>(bs.host.data())[o]
+                                                      : __half2float(reinterpret_cast<const __half*>(bs.host.data())[o]);
+            for (int kh = 0; kh < k; ++kh)
+                for (int kw = 0; kw < k; ++kw) {
+                    const int r = o + int(oc) * (kw + k * kh);
+                    br[r] = bv;
+                    for (int ic = 0; ic < kDim; ++ic)
+                        wr[size_t(r) * kDim + ic] = __float2half_rn(wval(size_t(ic) + kDim * (kw + k * (kh + size_t(k) * o))));
+                }
+        }
+        if (dev_alloc(c->allocs, &nf.w, wr.size() * 2) || dev_alloc(c->allocs, &nf.bias, br.size() * 4)) return -1;
+        S3T_CUDA(cudaMemcpy(nf.w, wr.data(), wr.size() * 2, cudaMemcpyHostToDevice));
+        S3T_CUDA(cudaMemcpy(nf.bias, br.data(), br.size() * 4, cudaMemcpyHostToDevice));
+        nf.oc = int(oc);
+        nf.rows = rows;
+    }
+    return 0;
+}
+
 }  // namespace
 
 int s3t::set_last_error(const char* msg) { return fail(msg); }
@@ -984,6 +1051,7 @@ int s3t_finalize_weights(s3t_ctx* c) {
                 if (!s || upload_f32_vec(c, *s, v.n, v.dst)) return -1;
             }
         }
+        if (prepare_neck(c)) return -1;
         S3T_CUDA(cudaStreamSynchronize(c->stream));
         for (auto& kv : c->staged)
             if (kv.second.dev) cudaFree(kv.second.dev);
@@ -1096,6 +1164,49 @@ int s3t_trunk_profile(s3t_ctx* c, const float* images_dev, int batch, float* out
         if (rc) return rc;
         S3T_CUDA(se);
         return check_status(c, st);
+    } S3T_CATCH_INT
+}
+
+int s3t_neck_first_shape(const s3t_ctx* c, int level, int64_t shape[4]) {
+    try {
+        if (!c || !shape) return fail("null argument to s3t_neck_first_shape");
+        if (!c->finalized) return fail("weights not finalized (call s3t_finalize_weights)");
+        if (level < 0 || level > 3) return fail("neck level must be in [0, 3]");
+        const auto& nf = c->neck[level];
+        if (!nf.w) return fail(nf.missing);
+        const int side = level < 2 ? 2 * kGrid : level == 2 ? kGrid : kGrid / 2;
+        shape[0] = 1;
+        shape[1] = nf.oc;
+        shape[2] = shape[3] = side;
+        return 0;
+    } S3T_CATCH_INT
+}
+
+int s3t_neck_first(s3t_ctx* c, int level, const float* trunk_dev, int batch, float* out_dev, void* stream) {
+    try {
+        if (!c) return fail("ctx is null");
+        if (!c->finalized) return fail("weights not finalized (call s3t_finalize_weights)");
+        if (!trunk_dev || !out_dev) return fail("trunk or out is null");
+        if (batch <= 0) return fail("batch must be positive");
+        if (level < 0 || level > 3) return fail("neck level must be in [0, 3]");
+        const auto& nf = c->neck[level];
+        if (!nf.w) return fail(nf.missing);
+        S3T_CUDA(cudaSetDevice(c->device));
+        cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+        if (ensure_workspace(c, batch)) return -1;   // a16 holds the A operand, h the GEMM result
+        const int T = level == 3 ? (kGrid / 2) * (kGrid / 2) : kTokens;
+        S3T_CUDA(launch_neck_tokens(trunk_dev, batch, level, c->a16, st));
+        GemmArgs g{};
+        g.M = batch * T;
+        g.N = nf.rows;
+        g.K = kDim;
+        g.bias = nf.bias;
+        g.out16 = c->h;
+        g.gelu = level == 0;
+        g.status = c->dev->status;
+        S3T_CUDA(launch_gemm(c->a16, nf.w, g, kEpiF16, c->dev->num_sms, st));
+        S3T_CUDA(launch_neck_out(c->h, batch, level, nf.oc, out_dev, st));
+        return 0;
     } S3T_CATCH_INT
 }
 
