@@ -490,6 +490,36 @@ def config_extras(torch, dev, stream, trunk, syn, s3t):
     except Exception as e:  # reported, not fatal for the headline line
         res["encoder_attention_error"] = str(e)
     res["rgb8"] = rgb8_extras(torch, dev, stream, trunk, s3t)
+    try:
+        res["neck_first"] = neck_extras(torch, dev, stream, syn, s3t)
+    except Exception as e:  # reported, not fatal for the headline line
+        res["neck_first_error"] = str(e)
+    return res
+
+
+def neck_extras(torch, dev, stream, syn, s3t, batch=8):
+    """The hand-off to the vision neck (s3t_neck_first): each level's first
+    operation on an 8-image trunk output left on the device (seeded F16 file
+    with the neck; 2 trunk layers, which do not change the neck's work)."""
+    model = s3t.GgufModel(syn.synthetic_gguf("f16", seed=0, layers=2, perturb=True, neck=True), device=dev.index)
+    trunk = s3t.VisionTrunk(model)
+    imgs = torch.from_numpy(syn.synthetic_images(batch)).to(dev)
+    feats = torch.empty((batch, 1024, 72, 72), device=dev)
+    trunk.run_device(imgs.data_ptr(), batch, feats.data_ptr(), stream.cuda_stream)
+    res = {"batch": batch}
+    for level in range(4):
+        shape = trunk.neck_first_shape(level)
+        out = torch.empty((batch,) + tuple(shape[1:]), device=dev)
+        fn = lambda: trunk.neck_first_device(level, feats.data_ptr(), batch, out.data_ptr(), stream.cuda_stream)
+        ms = _event_ms(torch, dev, stream, fn, 3, 20)
+        oc, side = shape[1], shape[2]
+        rows = oc * (4 if level < 2 else 1)
+        positions = (36 * 36 if level == 3 else 5184) * batch
+        flop = 2.0 * positions * 1024 * rows
+        res[f"level{level}"] = {"out": f"{batch}x{oc}x{side}x{side}", "ms": round(ms, 4),
+                                "tflops": round(flop / (ms / 1e3) / 1e12, 1)}
+    trunk.sync(stream.cuda_stream)
+    model.close()
     return res
 
 
