@@ -45,10 +45,11 @@ GEMM_FLOP_PER_IMAGE_LAYER = 144.05e9  # 2*T*C*(3C + C + 2F), T=5184, C=1024, F=4
 LAUNCHES_PER_TRUNK = 3 + 32 * 6 + 31  # im2col, patch GEMM, stem LN; 6 per block; 31 inter-block LNs
 GATHER_CHUNKS = 4                     # N > 1: pieces of a rank's shard whose gather overlaps the next piece
 # DRAM bytes (read + write) of the four GEMM launches of one block, per image:
-# one ncu capture of the four GEMM launches of block 0 of a 4-image trunk
-# (QKV 130 + proj 160 + fc1 197 + fc2 389 MB), scaled by the images a launch
-# processes.
-GEMM_DRAM_BYTES_PER_IMAGE_LAYER = 876e6 / 4
+# one ncu capture (dram__bytes_read.sum + dram__bytes_write.sum) of the four
+# GEMM launches of block 0 of a 16-image trunk, whose fp32 residual (340 MB)
+# is beyond the L2 (QKV 640 + proj 796 + fc1 913 + fc2 1703 MB;
+# profiles/gemm_pair_16img.md), scaled by the images a launch processes.
+GEMM_DRAM_BYTES_PER_IMAGE_LAYER = 4052e6 / 16
 
 
 def measured_peaks():
@@ -321,7 +322,8 @@ def _run_ours(a, torch, dist, world, rank, local, dev):
             "frac": round(achieved / bf16_peak, 4), "peak_kind": f"{peak_kind} bf16 burst",
             "frac_of_sustained": round(achieved / bf16_sus, 4) if bf16_sus else None,
             "traffic": GEMM_DRAM_BYTES_PER_IMAGE_LAYER * per,
-            "traffic_note": "bytes per block's four GEMM launches; ncu 4-image capture scaled by images",
+            "traffic_note": "DRAM bytes of one block's four GEMM launches: ncu capture at 16 images "
+                            "(profiles/gemm_pair_16img.md) scaled by images",
             "per_gemm_ms": {k: round(v, 4) for k, v in per_gemm.items()},
             "trunk_tensor_frac": round(FLOP_PER_IMAGE * value / world / 1e12 / bf16_peak, 4),
         },
