@@ -12,16 +12,22 @@
 // tile, head, group).  Roles (192 threads): warp 0 TMA producer, warp 1 TMEM
 // owner + UMMA issuer, warps 2..5 softmax + epilogue (one query row per
 // thread).  Per 64-key block b of an item:
-//   S = Q K^T   : UMMA M=128 N=64 K=64, accumulator in TMEM cols [0,64)
+//   S = Q K^T   : UMMA M=128 N=64 K=64, A = Q read from TMEM Q[item & 1],
+//                 K from shared memory, accumulator in TMEM cols [0,64)
 //   P = 2^(S*scale*log2e - m) as fp16/bf16 into TMEM P[b & 1] (32 columns)
 //   O += P V    : UMMA M=128 N=64 K=64, A = P read from TMEM, V MN-major from
-//                 shared memory, into TMEM O[item & 1]
-// The UMMA issuer runs one block ahead (S_{b+1} is issued as soon as S_b has
-// been read), across item boundaries too; P is double-buffered, so the
-// softmax of block b never waits for the PV of block b-1, and Q and O are
-// double-buffered so the next item's loads and first S overlap the current
-// item's epilogue.  P never touches shared memory (no proxy fence on the
-// critical path).  The row max used for P is raised only when a block
+//                 shared memory, into TMEM O
+// Both UMMA kinds take A from tensor memory, so each reads only its B tile
+// (2 KB per K step) from shared memory: an SS 128x64x16 UMMA, which also
+// reads the 4 KB Q slice every step, is bound by shared-memory bandwidth.
+// The softmax warps copy each item's Q tile from shared memory (TMA) into
+// Q[item & 1], the next item's while the current item's last block is
+// processed.  The UMMA issuer runs one block ahead (S_{b+1} is issued as soon
+// as S_b has been read), across item boundaries too; P is double-buffered, so
+// the softmax of block b never waits for the PV of block b-1.  O is single:
+// the next item's first PV needs P from the same warps, after their epilogue
+// has read O.  P never touches shared memory (no proxy fence on the critical
+// path).  The row max used for P is raised only when a block
 // exceeds it by more than 2^8 (O is then rescaled in TMEM).  Shared memory
 // (80 KB) and registers are sized for two CTAs per SM; a 3-deep K/V ring
 // keeps S_{b+1} from waiting on loads.
@@ -39,8 +45,10 @@ constexpr int kBQ = 128, kBKV = 64, kD = 64, kKVStages = 3;
 constexpr uint32_t kQBytes = kBQ * kD * 2;      // 16 KB
 constexpr uint32_t kKVBytes = kBKV * kD * 2;    // 8 KB (each of K, V)
 constexpr size_t kAttnSmem = 2 * kQBytes + 2 * kKVStages * kKVBytes + 1024 + 256;
-constexpr uint32_t kAttnTmemCols = 256;         // S [0,64), O0 [64,128), O1 [128,192), P0/P1 [192,256)
-constexpr uint32_t kTmemP = 192;                // P[x] at kTmemP + 32 x (64 fp16 keys per row)
+constexpr uint32_t kAttnTmemCols = 256;         // S [0,64), O [64,128), P0/P1 [128,192), Q0/Q1 [192,256)
+constexpr uint32_t kTmemO = 64;
+constexpr uint32_t kTmemP = 128;                // P[x] at kTmemP + 32 x (64 fp16 keys per row)
+constexpr uint32_t kTmemQ = 192;                // Q[x] at kTmemQ + 32 x (64 fp16 dims per row)
 constexpr int kCtasPerSm = 2;
 
 template <int BF16>
@@ -80,9 +88,10 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
     uint64_t* s_free = s_full + 1;
     uint64_t* p_full = s_free + 1;                   // [2]: P of blocks with that parity
     uint64_t* o_done = p_full + 2;                   // [2]: PV of blocks with that parity
-    uint64_t* o_free = o_done + 2;                   // [2]
-    uint64_t* drain = o_free + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    uint64_t* o_free = o_done + 2;                   // O read by the item epilogue
+    uint64_t* drain = o_free + 1;
+    uint64_t* qt_full = drain + 1;                   // [2]: Q of the item with that parity in TMEM
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(qt_full + 2);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -93,11 +102,12 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
     if (threadIdx.x == 0) {
         for (int i = 0; i < 2; ++i) {
             mbar_init(q_full + i, 1);
-            mbar_init(q_empty + i, 1);
-            mbar_init(o_free + i, 4);
+            mbar_init(q_empty + i, 4);
+            mbar_init(qt_full + i, 4);
             mbar_init(o_done + i, 1);
             mbar_init(p_full + i, 4);
         }
+        mbar_init(o_free, 4);
         for (int s = 0; s < kKVStages; ++s) {
             mbar_init(kv_full + s, 1);
             mbar_init(kv_empty + s, 1);
@@ -176,8 +186,6 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
             // Descriptors are built once; a K step of 16 advances the start
             // address field by 32 bytes (2) for K-major tiles and by 16 rows
             // of 128 bytes (128) for the MN-major V tile.
-            const uint64_t dQ0 = umma_desc_sw128(smem_u32(sQ), 16, 1024);
-            const uint64_t dQ1 = umma_desc_sw128(smem_u32(sQ + kQBytes), 16, 1024);
             const uint64_t dK0 = umma_desc_sw128(smem_u32(sK), 16, 1024);
             const uint64_t dV0 = umma_desc_sw128(smem_u32(sV), kKVBytes, 1024);
             constexpr uint64_t kStageStep = kKVBytes >> 4;
@@ -186,16 +194,18 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
             uint32_t sph = 0;
             auto issue_s = [&]() -> bool {
                 const int qb = sli & 1;
-                if (sj == 0 && !mbar_wait(q_full + qb, (sli >> 1) & 1, a.status, kErrTimeoutMma, abort_flag))
+                if (sj == 0 && !mbar_wait(qt_full + qb, (sli >> 1) & 1, a.status, kErrTimeoutMma, abort_flag))
                     return false;
                 if (!mbar_wait(kv_full + ss, sph, a.status, kErrTimeoutMma, abort_flag)) return false;
                 if (sb > 0 && !mbar_wait(s_free, (sb - 1) & 1, a.status, kErrTimeoutMma, abort_flag)) return false;
                 tc_fence_after();
-                const uint64_t dq = qb ? dQ1 : dQ0, dk = dK0 + uint64_t(ss) * kStageStep;
+                // S = Q K^T with Q read from tensor memory (TS form): only K
+                // comes from shared memory, so each UMMA reads half the bytes.
+                const uint32_t tq = tmem + kTmemQ + qb * 32;
+                const uint64_t dk = dK0 + uint64_t(ss) * kStageStep;
 #pragma unroll
-                for (int k = 0; k < kD / 16; ++k) umma_f16_ss(tS, dq + 2 * k, dk + 2 * k, idS, k != 0);
+                for (int k = 0; k < kD / 16; ++k) umma_f16_ts(tS, tq + 8 * k, dk + 2 * k, idS, k != 0);
                 umma_commit(s_full);
-                if (sj == nkv - 1) umma_commit(q_empty + qb);   // Q buffer reusable once these S complete
                 issued = true;
                 ++sb;
                 if (++sj == nkv) { sj = 0; ++sli; }
@@ -209,18 +219,17 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
                     ok = false;
                     break;
                 }
-                const int ob = li & 1;
                 if (!mbar_wait(p_full + (b & 1), (b >> 1) & 1, a.status, kErrTimeoutMma, abort_flag)) {
                     ok = false;
                     break;
                 }
-                if (j == 0 && !mbar_wait(o_free + ob, ((li >> 1) & 1) ^ 1, a.status, kErrTimeoutMma, abort_flag)) {
+                if (j == 0 && !mbar_wait(o_free, (li & 1) ^ 1, a.status, kErrTimeoutMma, abort_flag)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
                 const uint64_t dv = dV0 + uint64_t(s) * kStageStep;
-                const uint32_t tO = tmem + 64 + ob * 64;
+                const uint32_t tO = tmem + kTmemO;
                 const uint32_t tP = tmem + kTmemP + (b & 1) * 32;
 #pragma unroll
                 for (int k = 0; k < kBKV / 16; ++k) umma_f16_ts(tO, tP + 8 * k, dv + 128 * k, idO, (j | k) != 0);
@@ -246,10 +255,34 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
         constexpr float kRescaleSlack = 8.0f;
         bool ok = true;
         int b = 0, li = 0;
+        // Q of item i goes from its shared-memory tile (TMA, 128-byte swizzle)
+        // into tensor memory Q[i & 1], where the S UMMAs read it; the shared
+        // tile is then free for the producer.  Item 0 first, item i + 1 while
+        // item i's last block is processed (its S has been read).
+        auto copy_q = [&](int i) -> bool {
+            const int qb = i & 1;
+            if (!mbar_wait(q_full + qb, (i >> 1) & 1, a.status, kErrTimeoutEpilogue, abort_flag)) return false;
+            const uint8_t* rowp = sQ + qb * kQBytes + row * 128;
+            uint32_t qr[32];
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                const uint4 u = *reinterpret_cast<const uint4*>(rowp + ((c ^ (row & 7)) << 4));
+                qr[4 * c] = u.x; qr[4 * c + 1] = u.y; qr[4 * c + 2] = u.z; qr[4 * c + 3] = u.w;
+            }
+            tmem_st32(tmem + kTmemQ + qb * 32 + lane_off, qr);
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(qt_full + qb);
+                mbar_arrive(q_empty + qb);
+            }
+            return true;
+        };
+        if (int(blockIdx.x) < n_items) ok = copy_q(0);
+        const uint32_t tO = tmem + kTmemO;
         for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++li) {
             const Item it = item_of(w, n_qt);
-            const int ob = li & 1;
-            const uint32_t tO = tmem + 64 + ob * 64;
             float m_run = -INFINITY, l_run = 0.f;
             for (int j = 0; j < nkv; ++j, ++b) {
                 if (!mbar_wait(s_full, b & 1, a.status, kErrTimeoutEpilogue, abort_flag)) {
@@ -264,6 +297,10 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(s_free);
+                if (j == nkv - 1 && w + int(gridDim.x) < n_items && !copy_q(li + 1)) {
+                    ok = false;
+                    break;
+                }
 
                 float acc[8];
 #pragma unroll
@@ -342,7 +379,7 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
             tmem_wait_ld();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(o_free + ob);
+            if (lane == 0) mbar_arrive(o_free);
             const int qi = it.qt * kBQ + row;
             if (qi < a.L) {
                 const float inv = 1.0f / l_run;
