@@ -42,9 +42,10 @@ namespace s3t {
 namespace {
 
 constexpr int kBQ = 128, kBKV = 64, kD = 64, kKVStages = 3;
+constexpr int kQBufs = 2;                       // shared-memory Q tiles (TMA targets)
 constexpr uint32_t kQBytes = kBQ * kD * 2;      // 16 KB
 constexpr uint32_t kKVBytes = kBKV * kD * 2;    // 8 KB (each of K, V)
-constexpr size_t kAttnSmem = 2 * kQBytes + 2 * kKVStages * kKVBytes + 1024 + 256;
+constexpr size_t kAttnSmem = kQBufs * kQBytes + 2 * kKVStages * kKVBytes + 1024 + 256;
 constexpr uint32_t kAttnTmemCols = 256;         // S [0,64), O [64,128), P0/P1 [128,192), Q0/Q1 [192,256)
 constexpr uint32_t kTmemO = 64;
 constexpr uint32_t kTmemP = 128;                // P[x] at kTmemP + 32 x (64 fp16 keys per row)
@@ -76,8 +77,8 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
                     const __grid_constant__ CUtensorMap tmV, const AttnArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* sQ = smem;                              // 2 buffers
-    uint8_t* sK = sQ + 2 * kQBytes;
+    uint8_t* sQ = smem;                              // kQBufs buffers
+    uint8_t* sK = sQ + kQBufs * kQBytes;
     uint8_t* sV = sK + kKVStages * kKVBytes;
     uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kKVStages * kKVBytes);
     uint64_t* q_full = bars;                         // [2]
@@ -132,6 +133,8 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     const uint32_t tS = tmem;
+    griddep_launch_dependents();
+    griddep_wait();   // q, k, v are the QKV GEMM's output
 
     if (warp == 0) {
         if (lane == 0) {
@@ -142,8 +145,8 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
             for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++li) {
                 const Item it = item_of(w, n_qt);
                 const int bh = it.grp * kHeads + it.head;
-                const int qb = li & 1;
-                const uint32_t qph = (li >> 1) & 1;
+                const int qb = li % kQBufs;
+                const uint32_t qph = (li / kQBufs) & 1;
                 if (!mbar_wait(q_empty + qb, qph ^ 1, a.status, kErrTimeoutProducer, abort_flag)) {
                     ok = false;
                     break;
@@ -260,9 +263,9 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
         // tile is then free for the producer.  Item 0 first, item i + 1 while
         // item i's last block is processed (its S has been read).
         auto copy_q = [&](int i) -> bool {
-            const int qb = i & 1;
-            if (!mbar_wait(q_full + qb, (i >> 1) & 1, a.status, kErrTimeoutEpilogue, abort_flag)) return false;
-            const uint8_t* rowp = sQ + qb * kQBytes + row * 128;
+            const int qb = i & 1, qs = i % kQBufs;
+            if (!mbar_wait(q_full + qs, (i / kQBufs) & 1, a.status, kErrTimeoutEpilogue, abort_flag)) return false;
+            const uint8_t* rowp = sQ + qs * kQBytes + row * 128;
             uint32_t qr[32];
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
@@ -275,7 +278,7 @@ __global__ void __launch_bounds__(192, kCtasPerSm)
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive(qt_full + qb);
-                mbar_arrive(q_empty + qb);
+                mbar_arrive(q_empty + qs);
             }
             return true;
         };
@@ -445,11 +448,8 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t stream) {
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const int n_items = ((a.L + kBQ - 1) / kBQ) * kHeads * a.groups;
     const int grid = n_items < sms * kCtasPerSm ? n_items : sms * kCtasPerSm;
-    if (a.bf16)
-        attn_fwd_kernel<1><<<grid, 192, kAttnSmem, stream>>>(tq, tk, tv, a);
-    else
-        attn_fwd_kernel<0><<<grid, 192, kAttnSmem, stream>>>(tq, tk, tv, a);
-    return cudaGetLastError();
+    if (a.bf16) return launch_kernel(attn_fwd_kernel<1>, dim3(grid), dim3(192), kAttnSmem, stream, tq, tk, tv, a);
+    return launch_kernel(attn_fwd_kernel<0>, dim3(grid), dim3(192), kAttnSmem, stream, tq, tk, tv, a);
 }
 
 }  // namespace s3t

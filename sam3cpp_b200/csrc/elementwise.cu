@@ -75,6 +75,8 @@ __device__ __forceinline__ void load_row(const float* xr, int lane, float (&x)[3
 // +beta), producing the fp16 operand of the next GEMM.
 __global__ void __launch_bounds__(256) layernorm_kernel(const float* __restrict__ x, int rows, const float* g,
                                                         const float* b, __half* __restrict__ y, int q8) {
+    griddep_launch_dependents();
+    griddep_wait();
     const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (row >= rows) return;
     float v[32], o[32];
@@ -88,6 +90,8 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const float* __restrict_
 __global__ void __launch_bounds__(256) layernorm_stem_kernel(float* __restrict__ x, int rows, const float* g0,
                                                              const float* b0, const float* g1, const float* b1,
                                                              __half* __restrict__ y, int q8) {
+    griddep_launch_dependents();
+    griddep_wait();
     const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (row >= rows) return;
     float v[32], o[32];
@@ -106,6 +110,7 @@ __global__ void __launch_bounds__(256) layernorm_stem_kernel(float* __restrict__
 // ic*196 + kh*14 + kw (zero for the 52 pad columns up to 640).  One thread
 // writes 8 consecutive columns (16 bytes).
 __global__ void im2col_kernel(const float* __restrict__ img, int batch, __half* __restrict__ cols) {
+    griddep_launch_dependents();   // the patch GEMM's prologue overlaps this kernel
     const int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     const int64_t total = int64_t(batch) * kTokens * (kPatchKPad / 8);
     if (idx >= total) return;
@@ -191,14 +196,13 @@ __global__ void rope_kernel(T* x, int groups, int L, int windowed, const float* 
 
 cudaError_t launch_layernorm(const float* x, int rows, const float* g, const float* b, __half* y16, int q8,
                              cudaStream_t stream) {
-    layernorm_kernel<<<(rows + 7) / 8, 256, 0, stream>>>(x, rows, g, b, y16, q8);
-    return cudaGetLastError();
+    return launch_kernel(layernorm_kernel, dim3((rows + 7) / 8), dim3(256), 0, stream, x, rows, g, b, y16, q8);
 }
 
 cudaError_t launch_layernorm_stem(float* x, int rows, const float* g0, const float* b0, const float* g1,
                                   const float* b1, __half* y16, int q8, cudaStream_t stream) {
-    layernorm_stem_kernel<<<(rows + 7) / 8, 256, 0, stream>>>(x, rows, g0, b0, g1, b1, y16, q8);
-    return cudaGetLastError();
+    return launch_kernel(layernorm_stem_kernel, dim3((rows + 7) / 8), dim3(256), 0, stream, x, rows, g0, b0, g1, b1,
+                         y16, q8);
 }
 
 cudaError_t launch_im2col(const float* images, int batch, __half* cols, cudaStream_t stream) {

@@ -519,6 +519,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfgT<BK>::THREAD
     cluster_sync();   // both CTAs' barriers exist before any cross-CTA arrive
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    griddep_launch_dependents();
 
     if (warp == 0) {
         if (lane == 0) {
@@ -526,16 +527,37 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfgT<BK>::THREAD
             uint32_t ph = 0;
             uint32_t armed = 0, armed_parity = 0;
             bool ok = true;
+            // The weights do not depend on the previous kernel: the first
+            // tile's B tiles of the first stages are requested before
+            // griddep_wait, so they arrive while the predecessor drains.
+            int pre = 0;
+            if (pair < n_tiles) {
+                const int n0 = (pair % n_tiles_n) * BN + int(rank) * (BN / 2);
+                pre = num_kb < STAGES ? num_kb : STAGES;
+                for (int kb = 0; kb < pre; ++kb) {
+                    const uint32_t lfull = mapa_shared(smem_u32(full + kb), 0);
+                    if (leader) {
+                        mbar_arrive_expect_tx(full + kb, 2 * (Cfg::A_BYTES + Cfg::B_BYTES));
+                        armed |= 1u << kb;   // phase 0
+                    }
+#pragma unroll
+                    for (int at = 0; at < Cfg::BK / 64; ++at)
+                        tma_load_2d_pair(sB + kb * Cfg::B_BYTES + at * Cfg::ATOM_B, &tmB, lfull, kb * Cfg::BK + at * 64, n0);
+                }
+            }
+            griddep_wait();
             for (int tile = pair; tile < n_tiles && ok; tile += n_pairs) {
                 const int m0 = (tile / n_tiles_n) * 2 * kBM + int(rank) * kBM;
                 const int n0 = (tile % n_tiles_n) * BN + int(rank) * (BN / 2);
                 for (int kb = 0; kb < num_kb; ++kb) {
-                    if (!mbar_wait(empty + s, ph ^ 1, args.status, kErrTimeoutProducer, abort_flag)) {
+                    // Stages 0..pre-1 of the first tile: armed and B requested above.
+                    const bool prefetched = tile == pair && kb < pre;
+                    if (!prefetched && !mbar_wait(empty + s, ph ^ 1, args.status, kErrTimeoutProducer, abort_flag)) {
                         ok = false;
                         break;
                     }
                     const uint32_t lfull = mapa_shared(smem_u32(full + s), 0);
-                    if (leader) {
+                    if (leader && !prefetched) {
                         mbar_arrive_expect_tx(full + s, 2 * (Cfg::A_BYTES + Cfg::B_BYTES));
                         armed |= 1u << s;
                         armed_parity = (armed_parity & ~(1u << s)) | (ph << s);
@@ -543,7 +565,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfgT<BK>::THREAD
 #pragma unroll
                     for (int at = 0; at < Cfg::BK / 64; ++at) {
                         tma_load_2d_pair(sA + s * Cfg::A_BYTES + at * Cfg::ATOM_A, &tmA, lfull, kb * Cfg::BK + at * 64, m0);
-                        tma_load_2d_pair(sB + s * Cfg::B_BYTES + at * Cfg::ATOM_B, &tmB, lfull, kb * Cfg::BK + at * 64, n0);
+                        if (!prefetched)
+                            tma_load_2d_pair(sB + s * Cfg::B_BYTES + at * Cfg::ATOM_B, &tmB, lfull,
+                                             kb * Cfg::BK + at * 64, n0);
                     }
                     if (++s == STAGES) {
                         s = 0;
@@ -608,6 +632,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfgT<BK>::THREAD
     } else {
         // Epilogue warps 2..EPI_WARPS+1: warp w reads TMEM lane quarter w % 4
         // (rows 32*(w%4)..+31 of this CTA's half) and WARP_COLS of the 256 columns.
+        griddep_wait();   // the residual is the previous kernels' output
         const int quarter = warp & 3;
         const int col_grp = (warp - 2) >> 2;
         const int row = quarter * 32 + lane;
@@ -866,8 +891,8 @@ cudaError_t launch_pair_bk(const __half* A, const __half* B, const GemmArgs& arg
                           3 * uint64_t(args.qkv_stride) / (L * kHeadDim), 32, 8, CU_TENSOR_MAP_SWIZZLE_64B))
             return cudaErrorInvalidValue;
     }
-    gemm_pair_kernel<EPI, BK><<<2 * pairs, Cfg::THREADS, Cfg::template smem<EPI>(), stream>>>(ta, tb, tc, args);
-    return cudaGetLastError();
+    return launch_kernel(gemm_pair_kernel<EPI, BK>, dim3(2 * pairs), dim3(Cfg::THREADS), Cfg::template smem<EPI>(),
+                         stream, ta, tb, tc, args);
 }
 
 template <int EPI>

@@ -7,6 +7,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 namespace s3t {
 
 constexpr int kImage = 1008, kPatch = 14, kGrid = 72, kTokens = 5184, kDim = 1024;
@@ -50,6 +52,40 @@ struct GemmArgs {
     const float* rope_global_t; // [2][16][72]
     int* status;              // device status word
 };
+
+// Programmatic dependent launch for the trunk's chain of kernels.  While a
+// PdlScope(true) lives on this thread, the trunk launchers (pair GEMM,
+// attention, LayerNorm, im2col) add the programmatic-stream-serialization
+// attribute: a kernel is scheduled while its predecessor drains, runs its
+// prologue (barrier set-up, TMEM allocation, the first weight tiles) and then
+// waits in griddep_wait for the predecessor's results.  Off by default, so a
+// standalone op launch is ordered as usual.
+bool& pdl_enabled();
+struct PdlScope {
+    bool prev;
+    explicit PdlScope(bool on) : prev(pdl_enabled()) { pdl_enabled() = on; }
+    ~PdlScope() { pdl_enabled() = prev; }
+    PdlScope(const PdlScope&) = delete;
+    PdlScope& operator=(const PdlScope&) = delete;
+};
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                          Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    if (pdl_enabled()) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 // C[M,N] = A[M,K] * B[N,K]^T with A, B fp16 row-major (K contiguous).
 // Requires K % 64 == 0 and N % 32 == 0; A and B 16-byte aligned rows.

@@ -30,6 +30,16 @@ S3T_DEV void report_error(int* status, int code) {
     if (status) atomicCAS(status, 0, code);
 }
 
+// ------------------------------------------ programmatic dependent launch ---
+// griddep_wait: block until every grid this one depends on has completed and
+// its memory operations are visible; returns at once when the grid was
+// launched without programmatic stream serialization.  Every trunk kernel
+// calls it before its first read of a predecessor's output and before its
+// first global write.  griddep_launch_dependents: let the next grid of the
+// stream be scheduled (its CTAs run their prologue on free SMs, then wait).
+S3T_DEV void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+S3T_DEV void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ------------------------------------------------------------- mbarrier ---
 
 S3T_DEV void mbar_init(uint64_t* bar, uint32_t count) {

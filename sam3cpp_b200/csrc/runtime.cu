@@ -30,6 +30,11 @@
 
 using namespace s3t;
 
+bool& s3t::pdl_enabled() {
+    static thread_local bool on = false;
+    return on;
+}
+
 namespace {
 
 thread_local std::string g_last_error;
@@ -631,7 +636,11 @@ int trunk_graph(s3t_ctx* c, const float* din, int batch, int n_layers, float* do
         cudaStream_t cap;
         S3T_CUDA(cudaStreamCreateWithFlags(&cap, cudaStreamNonBlocking));
         S3T_CUDA(cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal));
-        const int rc = enqueue_trunk(c, din, batch, n_layers, dout, cap);
+        int rc;
+        {
+            PdlScope pdl(true);
+            rc = enqueue_trunk(c, din, batch, n_layers, dout, cap);
+        }
         cudaGraph_t graph = nullptr;
         const cudaError_t ec = cudaStreamEndCapture(cap, &graph);
         cudaStreamDestroy(cap);
