@@ -151,9 +151,11 @@ def _run_ours(a, torch, dist, world, rank, local, dev):
         raise SystemExit("--images must be divisible by --gpus")
     per = a.images // world
 
-    # model file: rank 0 writes it (cached), the others wait
+    # model files: rank 0 writes them (cached), the others wait
     if rank == 0:
         path = syn.synthetic_gguf(a.format)
+        if a.format == "f16" and not a.no_extras:
+            syn.synthetic_gguf("q8_0")
     if world > 1:
         dist.barrier()
     path = syn.synthetic_gguf(a.format)
@@ -169,16 +171,11 @@ def _run_ours(a, torch, dist, world, rank, local, dev):
     stream = torch.cuda.current_stream(dev)
     # N > 1: the shard runs in GATHER_CHUNKS pieces, and each piece's features
     # go to rank 0 (NCCL point-to-point) while the next piece computes.
-    chunks = [(i * per // GATHER_CHUNKS, (i + 1) * per // GATHER_CHUNKS) for i in range(GATHER_CHUNKS)]
-    chunks = [c for c in chunks if c[1] > c[0]] if world > 1 else [(0, per)]
+    chunks = shard_pieces(per, world)
     img_elems, out_elems = 3 * 1008 * 1008, 1024 * 72 * 72
 
     def gather_piece(i0, i1):
-        if rank == 0:
-            ops = [dist.P2POp(dist.irecv, gathered[r, i0:i1], r) for r in range(1, world)]
-        else:
-            ops = [dist.P2POp(dist.isend, out[i0:i1], 0)]
-        return dist.batch_isend_irecv(ops)
+        return gather_piece_to_rank0(rank, world, out, gathered, i0, i1)
 
     def step(gather=True):
         reqs = []
@@ -641,6 +638,29 @@ def run_reference(a):
         "e2e": {"value": round(value, 5), "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def shard_pieces(per: int, world: int, pieces: int = GATHER_CHUNKS) -> list[tuple[int, int]]:
+    """The [i0, i1) image ranges of one rank's shard of `per` images: one range
+    at N = 1, else up to `pieces` non-empty ranges whose gathers overlap the
+    next range's compute."""
+    if world <= 1:
+        return [(0, per)]
+    ranges = [(i * per // pieces, (i + 1) * per // pieces) for i in range(pieces)]
+    return [r for r in ranges if r[1] > r[0]]
+
+
+def gather_piece_to_rank0(rank: int, world: int, out, gathered, i0: int, i1: int):
+    """Images [i0, i1) of every rank's `out` [per, ...] into rank 0's
+    `gathered` [world, per, ...] (row r from rank r) by point-to-point sends;
+    returns the requests.  Rank 0's own rows are copied by the caller."""
+    import torch.distributed as dist
+
+    if rank == 0:
+        ops = [dist.P2POp(dist.irecv, gathered[r, i0:i1], r) for r in range(1, world)]
+    else:
+        ops = [dist.P2POp(dist.isend, out[i0:i1], 0)]
+    return dist.batch_isend_irecv(ops)
 
 
 def main():

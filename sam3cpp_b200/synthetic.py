@@ -171,7 +171,9 @@ def write_gguf(path: str | os.PathLike, weights: dict[str, np.ndarray], fmt: str
     from gguf import GGUFWriter, GGMLQuantizationType
 
     path = Path(path)
-    tmp = path.with_suffix(path.suffix + ".partial")
+    # A per-process partial name: processes that create the same file at once
+    # each write their own copy and the last atomic rename wins.
+    tmp = path.with_suffix(path.suffix + f".{os.getpid()}.partial")
     writer = GGUFWriter(str(tmp), arch="sam3")
     writer.add_int32("sam3.image_size", IMG)
     writer.add_int32("sam3.patch_size", PATCH)
@@ -190,10 +192,13 @@ def write_gguf(path: str | os.PathLike, weights: dict[str, np.ndarray], fmt: str
     writer.write_kv_data_to_file()
     writer.write_tensors_to_file()
     writer.close()
-    os.replace(tmp, path)
-    if hashed_names:
-        with open(str(path) + ".tensor_map.json", "w") as f:
+    if hashed_names:   # the sidecar first: a file that exists has its names
+        side = Path(str(path) + ".tensor_map.json")
+        side_tmp = side.with_suffix(f".{os.getpid()}.partial")
+        with open(side_tmp, "w") as f:
             json.dump(name_map, f, indent=2, sort_keys=True)
+        os.replace(side_tmp, side)
+    os.replace(tmp, path)
     return path
 
 
