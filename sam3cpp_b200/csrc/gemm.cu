@@ -465,7 +465,74 @@ struct PairCfgT {
 };
 using PairCfg = PairCfgT<128>;
 
-template <int EPI, int BK>
+// The work of one CTA pair, as segments of (tile, K blocks [k0, k1)).
+// Whole tiles: tile = pair, pair + n_pairs, ... with all K blocks.  Stream-K
+// (SK): the n_tiles x num_kb K-block units split into one contiguous range
+// per pair, each at least num_kb long, so a tile is shared by at most two
+// pairs.  A pair walks its range as: the head of the tile its range ends in
+// (K blocks [0, k1): kSegOut, first), its whole tiles, then the tail of the
+// tile its range starts in ([k0, num_kb): kSegIn, last).  The kSegOut
+// epilogue writes the raw accumulator to the pair's workspace slot and
+// raises one flag per epilogue warp; before the kSegIn mainloop, the
+// epilogue warps wait for the previous pair's flags and load that
+// accumulator into tensor memory, and the UMMAs continue on it.  Every
+// output is therefore the same sequential K accumulation as an unsplit
+// tile: results do not depend on stream-K, the batch or the timing.
+enum : int { kSegFull = 0, kSegOut = 1, kSegIn = 2 };
+struct Seg {
+    int tile, k0, k1, role;
+};
+struct SegWalk {
+    int num_kb, t, t_end, stride;
+    int head_tile, head_k1, tail_tile, tail_k0;
+    int phase;
+    __device__ SegWalk(int pair, int n_pairs, int n_tiles, int num_kb_, bool sk) : num_kb(num_kb_) {
+        if (!sk) {
+            t = pair; t_end = n_tiles; stride = n_pairs;
+            head_tile = tail_tile = -1;
+            head_k1 = tail_k0 = 0;
+            phase = 1;
+            return;
+        }
+        const int64_t units = int64_t(n_tiles) * num_kb;
+        const int u0 = int(units * pair / n_pairs), u1 = int(units * (pair + 1) / n_pairs);
+        head_k1 = u1 % num_kb;
+        head_tile = head_k1 ? u1 / num_kb : -1;
+        tail_k0 = u0 % num_kb;
+        tail_tile = tail_k0 ? u0 / num_kb : -1;
+        t = (u0 + num_kb - 1) / num_kb;
+        t_end = u1 / num_kb;
+        stride = 1;
+        phase = 0;
+    }
+    __device__ bool next(Seg& g) {
+        if (phase == 0) {
+            phase = 1;
+            if (head_tile >= 0) {
+                g.tile = head_tile; g.k0 = 0; g.k1 = head_k1; g.role = kSegOut;
+                return true;
+            }
+        }
+        if (phase == 1) {
+            if (t < t_end) {
+                g.tile = t; g.k0 = 0; g.k1 = num_kb; g.role = kSegFull;
+                t += stride;
+                return true;
+            }
+            phase = 2;
+        }
+        if (phase == 2) {
+            phase = 3;
+            if (tail_tile >= 0) {
+                g.tile = tail_tile; g.k0 = tail_k0; g.k1 = num_kb; g.role = kSegIn;
+                return true;
+            }
+        }
+        return false;
+    }
+};
+
+template <int EPI, int BK, bool SK>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfgT<BK>::THREADS, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmC, const GemmArgs args) {
@@ -482,7 +549,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfgT<BK>::THREAD
     uint64_t* tempty = tfull + 2;
     uint64_t* drain = tempty + 2;
     uint64_t* rload = drain + 1;                     // [EPI_WARPS]: residual chunk loads (kEpiResid)
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rload + Cfg::EPI_WARPS);
+    uint64_t* tpre = rload + Cfg::EPI_WARPS;         // stream-K: the kSegIn accumulator is loaded
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tpre + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -504,6 +572,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfgT<BK>::THREAD
         }
         mbar_init(drain, 1);
         for (int i = 0; i < Cfg::EPI_WARPS; ++i) mbar_init(rload + i, 1);
+        mbar_init(tpre, 2 * Cfg::EPI_WARPS);
         *abort_flag = 0;
         fence_barrier_init();
     }
@@ -528,30 +597,37 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfgT<BK>::THREAD
             uint32_t armed = 0, armed_parity = 0;
             bool ok = true;
             // The weights do not depend on the previous kernel: the first
-            // tile's B tiles of the first stages are requested before
+            // segment's B tiles of the first stages are requested before
             // griddep_wait, so they arrive while the predecessor drains.
+            SegWalk walk(pair, n_pairs, n_tiles, num_kb, SK);
             int pre = 0;
-            if (pair < n_tiles) {
-                const int n0 = (pair % n_tiles_n) * BN + int(rank) * (BN / 2);
-                pre = num_kb < STAGES ? num_kb : STAGES;
-                for (int kb = 0; kb < pre; ++kb) {
-                    const uint32_t lfull = mapa_shared(smem_u32(full + kb), 0);
-                    if (leader) {
-                        mbar_arrive_expect_tx(full + kb, 2 * (Cfg::A_BYTES + Cfg::B_BYTES));
-                        armed |= 1u << kb;   // phase 0
-                    }
+            {
+                SegWalk peek = walk;
+                Seg g0;
+                if (peek.next(g0)) {
+                    const int n0 = (g0.tile % n_tiles_n) * BN + int(rank) * (BN / 2);
+                    pre = g0.k1 - g0.k0 < STAGES ? g0.k1 - g0.k0 : STAGES;
+                    for (int i = 0; i < pre; ++i) {
+                        const uint32_t lfull = mapa_shared(smem_u32(full + i), 0);
+                        if (leader) {
+                            mbar_arrive_expect_tx(full + i, 2 * (Cfg::A_BYTES + Cfg::B_BYTES));
+                            armed |= 1u << i;   // phase 0
+                        }
 #pragma unroll
-                    for (int at = 0; at < Cfg::BK / 64; ++at)
-                        tma_load_2d_pair(sB + kb * Cfg::B_BYTES + at * Cfg::ATOM_B, &tmB, lfull, kb * Cfg::BK + at * 64, n0);
+                        for (int at = 0; at < Cfg::BK / 64; ++at)
+                            tma_load_2d_pair(sB + i * Cfg::B_BYTES + at * Cfg::ATOM_B, &tmB, lfull,
+                                             (g0.k0 + i) * Cfg::BK + at * 64, n0);
+                    }
                 }
             }
             griddep_wait();
-            for (int tile = pair; tile < n_tiles && ok; tile += n_pairs) {
-                const int m0 = (tile / n_tiles_n) * 2 * kBM + int(rank) * kBM;
-                const int n0 = (tile % n_tiles_n) * BN + int(rank) * (BN / 2);
-                for (int kb = 0; kb < num_kb; ++kb) {
-                    // Stages 0..pre-1 of the first tile: armed and B requested above.
-                    const bool prefetched = tile == pair && kb < pre;
+            Seg g;
+            for (bool first = true; ok && walk.next(g); first = false) {
+                const int m0 = (g.tile / n_tiles_n) * 2 * kBM + int(rank) * kBM;
+                const int n0 = (g.tile % n_tiles_n) * BN + int(rank) * (BN / 2);
+                for (int kb = g.k0; kb < g.k1; ++kb) {
+                    // Stages 0..pre-1 of the first segment: armed and B requested above.
+                    const bool prefetched = first && kb - g.k0 < pre;
                     if (!prefetched && !mbar_wait(empty + s, ph ^ 1, args.status, kErrTimeoutProducer, abort_flag)) {
                         ok = false;
                         break;
@@ -593,16 +669,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfgT<BK>::THREAD
             uint32_t ph = 0;
             bool ok = true, issued = false;
             int local = 0;
-            for (int tile = pair; tile < n_tiles && ok; tile += n_pairs, ++local) {
+            SegWalk walk(pair, n_pairs, n_tiles, num_kb, SK);
+            Seg g;
+            for (; ok && walk.next(g); ++local) {
                 const int acc = local & 1;
                 const uint32_t aph = (local >> 1) & 1;
                 if (!mbar_wait(tempty + acc, aph ^ 1, args.status, kErrTimeoutMma, abort_flag)) {
                     ok = false;
                     break;
                 }
+                // A kSegIn accumulator starts from the previous pair's partial,
+                // which the epilogue warps load into tensor memory.
+                if (SK && g.role == kSegIn && !mbar_wait(tpre, 0, args.status, kErrTimeoutMma, abort_flag)) {
+                    ok = false;
+                    break;
+                }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * BN;
-                for (int kb = 0; kb < num_kb; ++kb) {
+                const bool cont = SK && g.role == kSegIn;
+                for (int kb = g.k0; kb < g.k1; ++kb) {
                     if (!mbar_wait(full + s, ph, args.status, kErrTimeoutMma, abort_flag)) {
                         ok = false;
                         break;
@@ -613,7 +698,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfgT<BK>::THREAD
 #pragma unroll
                     for (int k = 0; k < Cfg::BK / 16; ++k)
                         umma_f16_ss_pair(d_tmem, da + (k / 4) * (Cfg::ATOM_A >> 4) + 2 * (k % 4),
-                                         db + (k / 4) * (Cfg::ATOM_B >> 4) + 2 * (k % 4), idesc, (kb | k) != 0);
+                                         db + (k / 4) * (Cfg::ATOM_B >> 4) + 2 * (k % 4), idesc,
+                                         cont || (kb != g.k0) || (k != 0));
                     issued = true;
                     umma_commit_pair(empty + s, 0x3);
                     if (++s == STAGES) {
@@ -639,12 +725,87 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfgT<BK>::THREAD
         uint32_t rphase = 0;     // parity of this warp's next residual load
         bool rpending = false;   // a residual load of this warp is in flight
         int local = 0;
-        for (int tile = pair; tile < n_tiles; tile += n_pairs, ++local) {
+        const int ew = warp - 2;
+        // This warp's 32 rows x WARP_COLS of a pair's stream-K slot: float4 i
+        // of chunk c of every lane at [(c * 8 + i) * 32 + lane], so each warp
+        // access is 512 contiguous bytes.
+        auto sk_slot = [&](int slot_pair) {
+            return args.sk_work + size_t(slot_pair) * kSkSlotFloats + int(rank) * (kSkSlotFloats / 2) +
+                   ew * (32 * Cfg::WARP_COLS) + lane * 4;
+        };
+        // Stream-K: the previous pair's head accumulator of the kSegIn tile
+        // into accumulator buffer `buf` (free: its last user's epilogue is done).
+        auto preload = [&](int buf) -> bool {
+            int* fl = args.sk_flags + ((pair - 1) * 2 + int(rank)) * 8 + ew;
+            int got = 1;
+            if (lane == 0) {
+                got = flag_wait(fl, args.status, kErrTimeoutEpilogue, abort_flag);
+                if (got) *fl = 0;   // consumed: zero again for the next launch
+            }
+            if (!__shfl_sync(0xffffffffu, got, 0)) return false;
+            const float* src = sk_slot(pair - 1);
+            const uint32_t tb = tmem_base + (uint32_t(quarter * 32) << 16) + buf * BN + col_grp * Cfg::WARP_COLS;
+#pragma unroll 1
+            for (int c = 0; c < Cfg::WARP_COLS / 32; ++c) {
+                uint32_t r[32];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const float4 v = __ldcg(reinterpret_cast<const float4*>(src + (c * 8 + i) * 128));
+                    r[4 * i] = __float_as_uint(v.x); r[4 * i + 1] = __float_as_uint(v.y);
+                    r[4 * i + 2] = __float_as_uint(v.z); r[4 * i + 3] = __float_as_uint(v.w);
+                }
+                tmem_st32(tb + c * 32, r);
+            }
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(tpre), 0));
+            return true;
+        };
+        SegWalk walk(pair, n_pairs, n_tiles, num_kb, SK);
+        Seg g, gnext;
+        bool have = walk.next(g);
+        if (SK && have && g.role == kSegIn && !preload(0)) have = false;
+        for (; have; g = gnext, ++local) {
+            const bool have_next = walk.next(gnext);
+            // The accumulator of a following kSegIn is loaded now, so its
+            // mainloop can overlap this segment's epilogue; after a kSegOut
+            // only once that segment's partial is out (pairs whose head is
+            // followed straight by their tail would otherwise wait in a chain).
+            const bool preload_next = SK && have_next && gnext.role == kSegIn;
+            if (preload_next && g.role != kSegOut && !preload((local + 1) & 1)) break;
+            const int tile = g.tile;
             const int acc = local & 1;
             const uint32_t aph = (local >> 1) & 1;
             const int m = (tile / n_tiles_n) * 2 * kBM + int(rank) * kBM + row;
             const int n0 = (tile % n_tiles_n) * BN + col_grp * Cfg::WARP_COLS;
             const bool row_ok = m < args.M;
+            if (SK && g.role == kSegOut) {
+                // The tile's first K blocks: raw accumulator to this pair's slot.
+                if (!mbar_wait(tfull + acc, aph, args.status, kErrTimeoutEpilogue, abort_flag)) break;
+                tc_fence_after();
+                const uint32_t tb = tmem_base + (uint32_t(quarter * 32) << 16) + acc * BN + col_grp * Cfg::WARP_COLS;
+                float* dst = sk_slot(pair);
+#pragma unroll 1
+                for (int c = 0; c < Cfg::WARP_COLS / 32; ++c) {
+                    uint32_t r[32];
+                    tmem_ld32(tb + c * 32, r);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        __stcg(reinterpret_cast<float4*>(dst + (c * 8 + i) * 128), make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
+                                                   __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3])));
+                }
+                __threadfence();
+                __syncwarp();
+                if (lane == 0) flag_release(args.sk_flags + (pair * 2 + int(rank)) * 8 + ew, 1);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(tempty + acc), 0));
+                if (preload_next && !preload((local + 1) & 1)) break;
+                have = have_next;
+                continue;
+            }
             if constexpr (EPI == kEpiResid) {
                 // The fp32 residual comes in by TMA, one 32 x 32 chunk at a time,
                 // into this warp's store stage: the first chunk while the tile's
@@ -812,6 +973,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfgT<BK>::THREAD
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(tempty + acc), 0));
+            have = have_next;
         }
         if constexpr (EPI == kEpiResid) {
             // Gave up mid-tile: let the residual load in flight land before the CTA exits.
@@ -873,7 +1035,23 @@ cudaError_t launch_pair_bk(const __half* A, const __half* B, const GemmArgs& arg
     const int n_tiles = ((args.M + 2 * kBM - 1) / (2 * kBM)) * ((args.N + PairCfg::BN - 1) / PairCfg::BN);
     // Persistent grid: only as many pairs as can be resident at once.
     const int max_pairs = g_pair_capacity > 0 ? g_pair_capacity : num_sms / 2;
-    const int pairs = n_tiles < max_pairs ? n_tiles : max_pairs;
+    int pairs = n_tiles < max_pairs ? n_tiles : max_pairs;
+    // Stream-K when whole tiles would leave the last of at most three waves
+    // mostly idle (one or two images: 84 or 164 fc2 tiles on 74 pairs) and
+    // the K loop is long enough to pay for the hand-over of a tile's
+    // accumulator (a K = 1024 tile's epilogue takes as long as its mainloop;
+    // at four images the hand-over costs more than the last wave's idle
+    // time); needs every pair resident, which the persistent grid of
+    // max_pairs is.
+    GemmArgs ka = args;
+    ka.sk = 0;
+    if (args.sk_work && args.sk_flags && args.sk_slots >= max_pairs && n_tiles >= max_pairs && args.K >= 2048) {
+        const int waves = (n_tiles + max_pairs - 1) / max_pairs;
+        if (waves <= 3 && int64_t(n_tiles) * 100 < int64_t(92) * waves * max_pairs) {
+            ka.sk = 1;
+            pairs = max_pairs;
+        }
+    }
     CUtensorMap tc = ta;
     if (EPI == kEpiF16 &&
         !make_tmap_2d(&tc, args.out16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, args.N, args.M, 32, 32,
@@ -891,8 +1069,11 @@ cudaError_t launch_pair_bk(const __half* A, const __half* B, const GemmArgs& arg
                           3 * uint64_t(args.qkv_stride) / (L * kHeadDim), 32, 8, CU_TENSOR_MAP_SWIZZLE_64B))
             return cudaErrorInvalidValue;
     }
-    return launch_kernel(gemm_pair_kernel<EPI, BK>, dim3(2 * pairs), dim3(Cfg::THREADS), Cfg::template smem<EPI>(),
-                         stream, ta, tb, tc, args);
+    if (ka.sk)
+        return launch_kernel(gemm_pair_kernel<EPI, BK, true>, dim3(2 * pairs), dim3(Cfg::THREADS),
+                             Cfg::template smem<EPI>(), stream, ta, tb, tc, ka);
+    return launch_kernel(gemm_pair_kernel<EPI, BK, false>, dim3(2 * pairs), dim3(Cfg::THREADS),
+                         Cfg::template smem<EPI>(), stream, ta, tb, tc, ka);
 }
 
 template <int EPI>
@@ -901,13 +1082,20 @@ cudaError_t launch_pair(const __half* A, const __half* B, const GemmArgs& args, 
                           : launch_pair_bk<EPI, 128>(A, B, args, num_sms, stream);
 }
 
-template <int EPI>
-cudaError_t prepare_pair() {
-    const cudaError_t e = cudaFuncSetAttribute(gemm_pair_kernel<EPI, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+template <int EPI, bool SK>
+cudaError_t prepare_pair_sk() {
+    const cudaError_t e = cudaFuncSetAttribute(gemm_pair_kernel<EPI, 128, SK>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                int(PairCfgT<128>::smem<EPI>()));
     if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(gemm_pair_kernel<EPI, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    return cudaFuncSetAttribute(gemm_pair_kernel<EPI, 64, SK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(PairCfgT<64>::smem<EPI>()));
+}
+
+template <int EPI>
+cudaError_t prepare_pair() {
+    const cudaError_t e = prepare_pair_sk<EPI, false>();
+    return e != cudaSuccess ? e : prepare_pair_sk<EPI, true>();
 }
 
 template <int BN, int EPI>
@@ -942,7 +1130,7 @@ cudaError_t gemm_prepare() {
         attr.val.clusterDim.z = 1;
         cfg.attrs = &attr;
         cfg.numAttrs = 1;
-        if (cudaOccupancyMaxActiveClusters(&clusters, gemm_pair_kernel<kEpiF16, 128>, &cfg) == cudaSuccess &&
+        if (cudaOccupancyMaxActiveClusters(&clusters, gemm_pair_kernel<kEpiF16, 128, false>, &cfg) == cudaSuccess &&
             clusters > 0)
             g_pair_capacity = clusters;
         else

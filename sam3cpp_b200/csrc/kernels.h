@@ -51,7 +51,16 @@ struct GemmArgs {
     const float* rope_local_t;  // the same tables transposed: [2][16][24]
     const float* rope_global_t; // [2][16][72]
     int* status;              // device status word
+    // Stream-K split of the pair kernel's K loop (null: whole tiles only).
+    // sk_work: kSkSlotFloats floats per CTA pair, sk_flags: kSkSlotFlags ints
+    // per CTA pair, all zero between launches.  sk is set by the launcher.
+    float* sk_work;
+    int* sk_flags;
+    int sk_slots;             // CTA pairs the two buffers have room for
+    int sk;
 };
+constexpr int kSkSlotFloats = 256 * 256;       // a pair's raw 256 x 256 fp32 accumulator
+constexpr int kSkSlotFlags = 2 * 8;            // one per epilogue warp of each CTA
 
 // Programmatic dependent launch for the trunk's chain of kernels.  While a
 // PdlScope(true) lives on this thread, the trunk launchers (pair GEMM,

@@ -95,6 +95,39 @@ S3T_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code, vo
     return mbar_wait_limit(bar, parity, status, code, abort, kWaitLimitNs);
 }
 
+// ------------------------------------------------------ global flags ---
+// A flag in global memory set by one CTA and awaited by another of the same
+// grid (both resident): release store / acquire load at GPU scope.
+
+S3T_DEV void flag_release(int* f, int v) {
+    asm volatile("st.release.gpu.global.s32 [%0], %1;" ::"l"(f), "r"(v) : "memory");
+}
+
+S3T_DEV int flag_acquire(const int* f) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+    return v;
+}
+
+// Bounded wait until *f != 0; false (with `code` recorded and *abort set) on
+// timeout, or when another role of the CTA already gave up.
+S3T_DEV bool flag_wait(const int* f, int* status, int code, volatile int* abort) {
+    if (flag_acquire(f)) return true;
+    const uint64_t t0 = globaltimer();
+    for (uint32_t i = 1;; ++i) {
+        if (flag_acquire(f)) return true;
+        __nanosleep(32);
+        if ((i & 63u) == 0) {
+            if (abort && *abort) return false;
+            if (globaltimer() - t0 > kWaitLimitNs) {
+                report_error(status, code);
+                if (abort) *abort = 1;
+                return false;
+            }
+        }
+    }
+}
+
 // ------------------------------------------------------------------ TMA ---
 
 S3T_DEV void tma_prefetch_desc(const CUtensorMap* map) {

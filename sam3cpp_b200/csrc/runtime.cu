@@ -398,9 +398,14 @@ struct s3t_ctx {
 
     int ws_batch = 0;
     std::vector<void*> ws_allocs;
+    std::vector<void*> sk_allocs;   // sk_work, sk_flags: independent of the batch
     float* x = nullptr;
     __half *a16 = nullptr, *qkv = nullptr, *attn = nullptr, *h = nullptr, *cols = nullptr;
     float *img = nullptr, *out = nullptr;
+    // Stream-K partials and flags of the pair GEMM (one slot per CTA pair).
+    float* sk_work = nullptr;
+    int* sk_flags = nullptr;
+    int sk_slots = 0;
     uint8_t* rgb = nullptr;   // device copy of host uint8 images (s3t_trunk_run_rgb8)
     size_t rgb_cap = 0;
 
@@ -459,7 +464,33 @@ int ensure_workspace(s3t_ctx* c, int batch) {
         free_workspace(c);
         return -1;
     }
+    if (!c->sk_work) {
+        const int slots = c->dev->num_sms / 2;
+        if (dev_alloc(c->sk_allocs, &c->sk_work, size_t(slots) * kSkSlotFloats * 4) ||
+            dev_alloc(c->sk_allocs, &c->sk_flags, size_t(slots) * kSkSlotFlags * 4)) {
+            for (void* q : c->sk_allocs) cudaFree(q);
+            c->sk_allocs.clear();
+            c->sk_work = nullptr;
+            c->sk_flags = nullptr;
+            free_workspace(c);
+            return -1;
+        }
+        S3T_CUDA(cudaMemset(c->sk_flags, 0, size_t(slots) * kSkSlotFlags * 4));
+        c->sk_slots = slots;
+    }
     c->ws_batch = batch;
+    return 0;
+}
+
+void use_stream_k(const s3t_ctx* c, GemmArgs& g) {
+    g.sk_work = c->sk_work;
+    g.sk_flags = c->sk_flags;
+    g.sk_slots = c->sk_slots;
+}
+
+// Stream-K flags back to zero (a run that gave up may have left some set).
+int reset_stream_k(const s3t_ctx* c, cudaStream_t st) {
+    S3T_CUDA(cudaMemsetAsync(c->sk_flags, 0, size_t(c->sk_slots) * kSkSlotFlags * 4, st));
     return 0;
 }
 
@@ -504,6 +535,7 @@ int enqueue_block(s3t_ctx* c, int l, int batch, float* out_nchw, cudaStream_t st
     q.rope_local_t = c->dev->rope_local_t;
     q.rope_global_t = c->dev->rope_global_t;
     q.status = status;
+    use_stream_k(c, q);
     S3T_CUDA(launch_gemm(c->a16, w.qkv, q, kEpiQkv, sms, st));
     S3T_MARK(kProfQkv);
 
@@ -527,6 +559,7 @@ int enqueue_block(s3t_ctx* c, int l, int batch, float* out_nchw, cudaStream_t st
     p.bias = w.proj_b;
     p.resid = c->x;
     p.status = status;
+    use_stream_k(c, p);
     S3T_CUDA(launch_gemm(c->attn, w.proj, p, kEpiResid, sms, st));
     S3T_MARK(kProfProj);
 
@@ -540,6 +573,7 @@ int enqueue_block(s3t_ctx* c, int l, int batch, float* out_nchw, cudaStream_t st
     f1.gelu = 1;
     f1.q8 = w.fc2_t == S3T_TYPE_Q8_0;
     f1.status = status;
+    use_stream_k(c, f1);
     S3T_CUDA(launch_gemm(c->a16, w.fc1, f1, kEpiF16, sms, st));
     S3T_MARK(kProfFc1);
 
@@ -549,6 +583,7 @@ int enqueue_block(s3t_ctx* c, int l, int batch, float* out_nchw, cudaStream_t st
     f2.resid = c->x;
     f2.out_nchw = out_nchw;
     f2.status = status;
+    use_stream_k(c, f2);
     S3T_CUDA(launch_gemm(c->h, w.fc2, f2, kEpiResid, sms, st));
     S3T_MARK(kProfFc2);
 
@@ -560,6 +595,7 @@ int enqueue_trunk(s3t_ctx* c, const float* images, int batch, int n_layers, floa
     const int sms = c->dev->num_sms;
     int* status = c->dev->status;
     S3T_CUDA(cudaMemsetAsync(status, 0, sizeof(int), st));
+    if (reset_stream_k(c, st)) return -1;
     S3T_MARK(-1);
     S3T_CUDA(launch_im2col(images, batch, c->cols, st));
 
@@ -570,6 +606,7 @@ int enqueue_trunk(s3t_ctx* c, const float* images, int batch, int n_layers, floa
     g.resid = c->x;
     g.pos = c->pos;
     g.status = status;
+    use_stream_k(c, g);
     S3T_CUDA(launch_gemm(c->cols, c->patch_w, g, kEpiPatch, sms, st));
     S3T_CUDA(launch_layernorm_stem(c->x, M, c->lnpre_w, c->lnpre_b, c->layers[0].n1w, c->layers[0].n1b, c->a16,
                                    c->layers[0].qkv_t == S3T_TYPE_Q8_0, st));
@@ -893,6 +930,7 @@ void s3t_destroy(s3t_ctx* c) {
         cudaSetDevice(c->device);
         cudaStreamSynchronize(c->stream);
         free_workspace(c);
+        for (void* p : c->sk_allocs) cudaFree(p);
         for (auto& kv : c->staged)
             if (kv.second.dev) cudaFree(kv.second.dev);
         for (void* p : c->allocs) cudaFree(p);
@@ -1099,6 +1137,7 @@ int s3t_trunk_run_block(s3t_ctx* c, int layer, const float* x_dev, int batch, fl
         const int M = batch * kTokens;
         const LayerW& w = c->layers[layer];
         S3T_CUDA(cudaMemsetAsync(c->dev->status, 0, sizeof(int), st));
+        if (reset_stream_k(c, st)) return -1;
         S3T_CUDA(cudaMemcpyAsync(c->x, x_dev, size_t(M) * kDim * 4, cudaMemcpyDeviceToDevice, st));
         S3T_CUDA(launch_layernorm(c->x, M, w.n1w, w.n1b, c->a16, w.qkv_t == S3T_TYPE_Q8_0, st));
         if (enqueue_block(c, layer, batch, nullptr, st)) return -1;

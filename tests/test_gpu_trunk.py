@@ -79,15 +79,21 @@ def test_eight_layers_with_global(gpu, oracle, fmt):
 
 
 def test_batch_matches_single(gpu):
-    """Images of a batch are independent: batch-3 output equals three batch-1 runs."""
+    """Images of a batch are independent: batch-3 and batch-2 outputs equal
+    batch-1 runs bit for bit.  One and two images run fc2 stream-K (84 and 164
+    tiles on the CTA pairs, split at different K blocks), three images whole
+    tiles: the accumulator hand-over keeps the K sum sequential."""
     from sam3cpp_b200 import synthetic as s
     path, _ = _models("f16", 2, True)
     trunk = gpu.VisionTrunk(gpu.GgufModel(path))
     imgs = s.synthetic_images(3)
     batched = trunk.run_batch(imgs)
+    pair = trunk.run_batch(imgs[1:3])
     for i in range(3):
         single = trunk.run_batch(imgs[i:i + 1])
         assert np.array_equal(batched[i], single[0])
+        if i:
+            assert np.array_equal(pair[i - 1], single[0])
 
 
 def test_host_pipelined_batch_matches_single(gpu):

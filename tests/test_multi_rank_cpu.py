@@ -29,18 +29,19 @@ def _free_port() -> int:
 
 def test_shard_pieces():
     b = _bench()
-    assert b.shard_pieces(32, 1) == [(0, 32)]
+    assert b.shard_pieces(64, 1) == [(0, 64)]
     assert b.shard_pieces(32, 2) == [(0, 8), (8, 16), (16, 24), (24, 32)]
-    assert b.shard_pieces(8, 8) == [(0, 2), (2, 4), (4, 6), (6, 8)]
+    assert b.shard_pieces(16, 4) == [(0, 8), (8, 16)]
+    assert b.shard_pieces(8, 8) == [(0, 8)]
     assert b.shard_pieces(1, 8) == [(0, 1)]
-    assert b.shard_pieces(3, 2) == [(0, 1), (1, 2), (2, 3)]
+    assert b.shard_pieces(20, 2, pieces=4) == [(0, 10), (10, 20)]
     for per in range(1, 40):
         pieces = b.shard_pieces(per, 4)
         assert pieces[0][0] == 0 and pieces[-1][1] == per
         assert all(p[1] == q[0] for p, q in zip(pieces, pieces[1:]))
 
 
-def _gather_worker(rank, world, port, per, q):
+def _gather_worker(rank, world, port, per, q, pieces):
     import torch
     import torch.distributed as dist
 
@@ -54,7 +55,7 @@ def _gather_worker(rank, world, port, per, q):
         out = torch.arange(np.prod(shape), dtype=torch.float32).reshape(shape) + 1000.0 * rank
         gathered = torch.full((world,) + shape, -1.0) if rank == 0 else None
         reqs = []
-        for i0, i1 in b.shard_pieces(per, world):
+        for i0, i1 in b.shard_pieces(per, world, pieces):
             reqs += b.gather_piece_to_rank0(rank, world, out, gathered, i0, i1)
         for r in reqs:
             r.wait()
@@ -68,14 +69,14 @@ def _gather_worker(rank, world, port, per, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("per", [5, 8])
-def test_chunked_gather_gloo_world2(per):
+@pytest.mark.parametrize("per,pieces", [(5, 1), (16, 2), (32, 4)])
+def test_chunked_gather_gloo_world2(per, pieces):
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_gather_worker, args=(r, 2, port, per, q)) for r in range(2)]
+    procs = [ctx.Process(target=_gather_worker, args=(r, 2, port, per, q, pieces)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
