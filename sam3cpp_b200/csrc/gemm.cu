@@ -434,7 +434,7 @@ __global__ void __launch_bounds__(192, 1)
 // outputs (fp16 for kEpiF16 / kEpiQkv, the fp32 residual for kEpiResid) leave
 // through shared memory and one TMA store per 32 x 32 chunk instead of 32
 // scattered row stores.
-template <int BK_>
+template <int BK_, int RBUF_ = 1>
 struct PairCfgT {
     static constexpr int BN = 256;
     // A stage holds BK K-columns as 64-column (128-byte) swizzle atoms.  With
@@ -457,9 +457,21 @@ struct PairCfgT {
         return EPI == kEpiF16 || EPI == kEpiQkv || EPI == kEpiResid;
     }
     static constexpr uint32_t OUT_BYTES = OUT_BUFS * 2048;
+    // The residual epilogue (kEpiResid, 64-column stages) keeps RBUF 32 x 32
+    // fp32 chunks per warp in flight.  Two (proj: its epilogue is as long as
+    // its K = 1024 mainloop, and exposed at one or two images) cost 32 KB,
+    // paid for with a 5-deep ring; the long-K fc2 keeps one and 6 stages.
+    static constexpr int RBUF = RBUF_;
+    static constexpr uint32_t kResidBuf = 32 * 32 * 4;
+    __host__ __device__ static constexpr int stages(int EPI) {
+        return EPI == kEpiResid && RBUF_ == 2 ? 5 : STAGES;
+    }
+    __host__ __device__ static constexpr uint32_t out_bytes(int EPI) {
+        return EPI == kEpiResid ? RBUF_ * kResidBuf : (staged_out(EPI) ? OUT_BYTES : 0);
+    }
     template <int EPI>
     static constexpr size_t smem() {
-        return size_t(STAGES) * (A_BYTES + B_BYTES) + (staged_out(EPI) ? EPI_WARPS * OUT_BYTES : 0) + 1024 + 256;
+        return size_t(stages(EPI)) * (A_BYTES + B_BYTES) + EPI_WARPS * out_bytes(EPI) + 1024 + 512;
     }
     static constexpr int THREADS = 64 + 32 * EPI_WARPS;
 };
@@ -532,24 +544,26 @@ struct SegWalk {
     }
 };
 
-template <int EPI, int BK, bool SK>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfgT<BK>::THREADS, 1)
+template <int EPI, int BK, bool SK, int RB>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfgT<BK, RB>::THREADS, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmC, const GemmArgs args) {
-    using Cfg = PairCfgT<BK>;
-    constexpr int STAGES = Cfg::STAGES, BN = Cfg::BN;
+    using Cfg = PairCfgT<BK, RB>;
+    static_assert(RB == 1 || (EPI == kEpiResid && BK == 64), "two residual buffers fit beside 64-column stages only");
+    constexpr int STAGES = Cfg::stages(EPI), BN = Cfg::BN;
+    constexpr uint32_t OUTB = Cfg::out_bytes(EPI);
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
     uint8_t* sB = smem + STAGES * Cfg::A_BYTES;
     uint8_t* sOut = sB + STAGES * Cfg::B_BYTES;
-    uint64_t* full = reinterpret_cast<uint64_t*>(sOut + (Cfg::staged_out(EPI) ? Cfg::EPI_WARPS * Cfg::OUT_BYTES : 0));
+    uint64_t* full = reinterpret_cast<uint64_t*>(sOut + Cfg::EPI_WARPS * OUTB);
     uint64_t* empty = full + STAGES;
     uint64_t* tfull = empty + STAGES;
     uint64_t* tempty = tfull + 2;
     uint64_t* drain = tempty + 2;
-    uint64_t* rload = drain + 1;                     // [EPI_WARPS]: residual chunk loads (kEpiResid)
-    uint64_t* tpre = rload + Cfg::EPI_WARPS;         // stream-K: the kSegIn accumulator is loaded
+    uint64_t* rload = drain + 1;                     // [EPI_WARPS][2]: residual chunk loads (kEpiResid)
+    uint64_t* tpre = rload + 2 * Cfg::EPI_WARPS;     // stream-K: the kSegIn accumulator is loaded
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tpre + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -571,7 +585,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfgT<BK>::THREAD
             mbar_init(tempty + i, 2 * Cfg::EPI_WARPS);   // every epilogue warp of the pair
         }
         mbar_init(drain, 1);
-        for (int i = 0; i < Cfg::EPI_WARPS; ++i) mbar_init(rload + i, 1);
+        for (int i = 0; i < 2 * Cfg::EPI_WARPS; ++i) mbar_init(rload + i, 1);
         mbar_init(tpre, 2 * Cfg::EPI_WARPS);
         *abort_flag = 0;
         fence_barrier_init();
@@ -722,8 +736,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfgT<BK>::THREAD
         const int quarter = warp & 3;
         const int col_grp = (warp - 2) >> 2;
         const int row = quarter * 32 + lane;
-        uint32_t rphase = 0;     // parity of this warp's next residual load
-        bool rpending = false;   // a residual load of this warp is in flight
+        uint32_t rphase = 0;     // bit b: parity of the next residual load into buffer b
+        uint32_t rpending = 0;   // bit b: a residual load into buffer b is in flight
         int local = 0;
         const int ew = warp - 2;
         // This warp's 32 rows x WARP_COLS of a pair's stream-K slot: float4 i
@@ -807,22 +821,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfgT<BK>::THREAD
                 continue;
             }
             if constexpr (EPI == kEpiResid) {
-                // The fp32 residual comes in by TMA, one 32 x 32 chunk at a time,
-                // into this warp's store stage: the first chunk while the tile's
+                // The fp32 residual comes in by TMA, 32 x 32 chunks into this
+                // warp's RB store stages: the first RB chunks while the tile's
                 // mainloop still runs, the others pulled into L2 now and loaded
-                // as soon as the previous chunk's store has read the stage (the
-                // residual is not written by anyone else before this epilogue).
+                // into a stage as soon as its store has read it, RB chunks
+                // ahead (the residual is not written by anyone else before this
+                // epilogue).
                 const int row0 = m - lane;
                 if (*abort_flag) break;
                 if (row0 < args.M) {
                     if (lane == 0) {
-                        bulk_wait_group_read<0>();
-                        mbar_arrive_expect_tx(rload + (warp - 2), 32 * 32 * 4);
-                        tma_load_2d(sOut + (warp - 2) * Cfg::OUT_BYTES, &tmC, rload + (warp - 2), n0, row0);
+                        bulk_wait_group_read<0>();   // the previous tile's stores have read both stages
 #pragma unroll
-                        for (int q = 1; q < Cfg::WARP_COLS / 32; ++q) tma_prefetch_l2_2d(&tmC, n0 + 32 * q, row0);
+                        for (int b = 0; b < RB; ++b) {
+                            mbar_arrive_expect_tx(rload + 2 * ew + b, Cfg::kResidBuf);
+                            tma_load_2d(sOut + ew * OUTB + b * Cfg::kResidBuf, &tmC, rload + 2 * ew + b, n0 + 32 * b,
+                                        row0);
+                        }
+#pragma unroll
+                        for (int q = RB; q < Cfg::WARP_COLS / 32; ++q) tma_prefetch_l2_2d(&tmC, n0 + 32 * q, row0);
                     }
-                    rpending = true;
+                    rpending = (1u << RB) - 1;
                 }
             }
             if (!mbar_wait(tfull + acc, aph, args.status, kErrTimeoutEpilogue, abort_flag)) break;
@@ -831,7 +850,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfgT<BK>::THREAD
             if constexpr (EPI == kEpiF16) {
                 // Rows row0..row0+31 of the chunk go out through shared memory
                 // and one TMA store per warp (rows past M are not written).
-                uint8_t* stage = sOut + (warp - 2) * Cfg::OUT_BYTES;
+                uint8_t* stage = sOut + (warp - 2) * OUTB;
                 const int row0 = m - lane;
 #pragma unroll 1
                 for (int c = 0; c < Cfg::WARP_COLS / 32; ++c) {
@@ -862,7 +881,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfgT<BK>::THREAD
                 // As above, but a 32-row chunk is stored as four 8-row boxes
                 // into the [which][group][head][token][64] layout: 8 tokens in
                 // a row of the grid never straddle a window or an image.
-                uint8_t* stage = sOut + (warp - 2) * Cfg::OUT_BYTES;
+                uint8_t* stage = sOut + (warp - 2) * OUTB;
                 const int row0 = m - lane;
                 const int L = args.windowed ? kWindow * kWindow : kTokens;
                 const int planes = int(args.qkv_stride / (int64_t(L) * kHeadDim));   // group x head planes per q/k/v
@@ -901,12 +920,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfgT<BK>::THREAD
                     }
                 }
             } else if constexpr (EPI == kEpiResid) {
-                // The stage (32 rows x 128 B, 128-byte swizzle, the layout TMA
+                // Stage c % RB (32 rows x 128 B, 128-byte swizzle, the layout TMA
                 // writes) holds chunk c of the residual; each lane adds its row's
                 // accumulator and bias in place, and one TMA store writes the
                 // chunk back.  Rows past M are zero-filled by the load and not
                 // written by the store.
-                uint8_t* stage = sOut + (warp - 2) * Cfg::OUT_BYTES;
                 const int row0 = m - lane;
                 const bool chunk_rows = row0 < args.M;   // warp-uniform
                 // A warp whose 32 rows all lie past M has nothing to add or store;
@@ -918,9 +936,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfgT<BK>::THREAD
                     uint32_t r[32];
                     tmem_ld32(tbase + c * 32, r);
                     tmem_wait_ld();
-                    if (!mbar_wait(rload + (warp - 2), rphase, args.status, kErrTimeoutEpilogue, abort_flag)) break;
-                    rphase ^= 1;
-                    rpending = false;
+                    const int b = c % RB;
+                    uint8_t* stage = sOut + ew * OUTB + b * Cfg::kResidBuf;
+                    if (!mbar_wait(rload + 2 * ew + b, (rphase >> b) & 1u, args.status, kErrTimeoutEpilogue, abort_flag))
+                        break;
+                    rphase ^= 1u << b;
+                    rpending &= ~(1u << b);
                     uint8_t* rowp = stage + lane * 128;
                     // x = x + (acc + bias), two columns per packed operation
                     const float4* bp = reinterpret_cast<const float4*>(args.bias + n);
@@ -945,13 +966,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfgT<BK>::THREAD
                     if (lane == 0) {
                         tma_store_2d(&tmC, stage, n, row0);
                         bulk_commit_group();
-                        if (c + 1 < Cfg::WARP_COLS / 32) {
+                        if (c + RB < Cfg::WARP_COLS / 32) {
                             bulk_wait_group_read<0>();   // the store has read the stage
-                            mbar_arrive_expect_tx(rload + (warp - 2), 32 * 32 * 4);
-                            tma_load_2d(stage, &tmC, rload + (warp - 2), n + 32, row0);
+                            mbar_arrive_expect_tx(rload + 2 * ew + b, Cfg::kResidBuf);
+                            tma_load_2d(stage, &tmC, rload + 2 * ew + b, n + 32 * RB, row0);
                         }
                     }
-                    rpending = c + 1 < Cfg::WARP_COLS / 32;
+                    if (c + RB < Cfg::WARP_COLS / 32) rpending |= 1u << b;
                     if (row_ok && args.out_nchw) {
                         const int img = m / kTokens, t = m - img * kTokens;
                         float* o = args.out_nchw + (int64_t(img) * args.N + n) * kTokens + t;
@@ -976,8 +997,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfgT<BK>::THREAD
             have = have_next;
         }
         if constexpr (EPI == kEpiResid) {
-            // Gave up mid-tile: let the residual load in flight land before the CTA exits.
-            if (rpending) mbar_wait(rload + (warp - 2), rphase, args.status, kErrTimeoutDrain, nullptr);
+            // Gave up mid-tile: let the residual loads in flight land before the CTA exits.
+            for (int b = 0; b < 2; ++b)
+                if (rpending & (1u << b))
+                    mbar_wait(rload + 2 * ew + b, (rphase >> b) & 1u, args.status, kErrTimeoutDrain, nullptr);
         }
         if constexpr (Cfg::staged_out(EPI)) {
             if (lane == 0) bulk_wait_group_all();
@@ -1025,9 +1048,9 @@ cudaError_t launch_bn(const __half* A, const __half* B, const GemmArgs& args, in
 // gemm_prepare; one process drives one device at a time in this library).
 int g_pair_capacity = 0;
 
-template <int EPI, int BK>
+template <int EPI, int BK, int RB = 1>
 cudaError_t launch_pair_bk(const __half* A, const __half* B, const GemmArgs& args, int num_sms, cudaStream_t stream) {
-    using Cfg = PairCfgT<BK>;
+    using Cfg = PairCfgT<BK, RB>;
     CUtensorMap ta, tb;
     if (!make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, args.K, args.M, kBK, kBM)) return cudaErrorInvalidValue;
     if (!make_tmap_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, args.K, args.N, kBK, PairCfg::BN / 2))
@@ -1070,25 +1093,36 @@ cudaError_t launch_pair_bk(const __half* A, const __half* B, const GemmArgs& arg
             return cudaErrorInvalidValue;
     }
     if (ka.sk)
-        return launch_kernel(gemm_pair_kernel<EPI, BK, true>, dim3(2 * pairs), dim3(Cfg::THREADS),
+        return launch_kernel(gemm_pair_kernel<EPI, BK, true, RB>, dim3(2 * pairs), dim3(Cfg::THREADS),
                              Cfg::template smem<EPI>(), stream, ta, tb, tc, ka);
-    return launch_kernel(gemm_pair_kernel<EPI, BK, false>, dim3(2 * pairs), dim3(Cfg::THREADS),
+    return launch_kernel(gemm_pair_kernel<EPI, BK, false, RB>, dim3(2 * pairs), dim3(Cfg::THREADS),
                          Cfg::template smem<EPI>(), stream, ta, tb, tc, ka);
 }
 
 template <int EPI>
 cudaError_t launch_pair(const __half* A, const __half* B, const GemmArgs& args, int num_sms, cudaStream_t stream) {
-    return args.K >= 2048 ? launch_pair_bk<EPI, 64>(A, B, args, num_sms, stream)
-                          : launch_pair_bk<EPI, 128>(A, B, args, num_sms, stream);
+    if constexpr (EPI == kEpiResid)
+        return args.K >= 2048 ? launch_pair_bk<EPI, 64, 1>(A, B, args, num_sms, stream)
+                              : launch_pair_bk<EPI, 64, 2>(A, B, args, num_sms, stream);
+    else
+        return args.K >= 2048 ? launch_pair_bk<EPI, 64>(A, B, args, num_sms, stream)
+                              : launch_pair_bk<EPI, 128>(A, B, args, num_sms, stream);
 }
 
 template <int EPI, bool SK>
 cudaError_t prepare_pair_sk() {
-    const cudaError_t e = cudaFuncSetAttribute(gemm_pair_kernel<EPI, 128, SK>,
-                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               int(PairCfgT<128>::smem<EPI>()));
-    if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(gemm_pair_kernel<EPI, 64, SK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if constexpr (EPI == kEpiResid) {
+        const cudaError_t e = cudaFuncSetAttribute(gemm_pair_kernel<EPI, 64, SK, 2>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   int(PairCfgT<64, 2>::smem<EPI>()));
+        if (e != cudaSuccess) return e;
+    } else {
+        const cudaError_t e = cudaFuncSetAttribute(gemm_pair_kernel<EPI, 128, SK, 1>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   int(PairCfgT<128>::smem<EPI>()));
+        if (e != cudaSuccess) return e;
+    }
+    return cudaFuncSetAttribute(gemm_pair_kernel<EPI, 64, SK, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(PairCfgT<64>::smem<EPI>()));
 }
 
@@ -1130,7 +1164,7 @@ cudaError_t gemm_prepare() {
         attr.val.clusterDim.z = 1;
         cfg.attrs = &attr;
         cfg.numAttrs = 1;
-        if (cudaOccupancyMaxActiveClusters(&clusters, gemm_pair_kernel<kEpiF16, 128, false>, &cfg) == cudaSuccess &&
+        if (cudaOccupancyMaxActiveClusters(&clusters, gemm_pair_kernel<kEpiF16, 128, false, 1>, &cfg) == cudaSuccess &&
             clusters > 0)
             g_pair_capacity = clusters;
         else
