@@ -48,9 +48,9 @@ MIN_PIECE = 8                         # ... each of at least this many images
 # DRAM bytes (read + write) of the four GEMM launches of one block, per image:
 # one ncu capture (dram__bytes_read.sum + dram__bytes_write.sum) of the four
 # GEMM launches of block 0 of a 16-image trunk, whose fp32 residual (340 MB)
-# is beyond the L2 (QKV 640 + proj 796 + fc1 913 + fc2 1703 MB;
+# is beyond the L2 (QKV 643 + proj 796 + fc1 916 + fc2 1752 MB;
 # profiles/gemm_pair_16img.md), scaled by the images a launch processes.
-GEMM_DRAM_BYTES_PER_IMAGE_LAYER = 4052e6 / 16
+GEMM_DRAM_BYTES_PER_IMAGE_LAYER = 4107e6 / 16
 
 
 def measured_peaks():
