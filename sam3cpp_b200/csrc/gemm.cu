@@ -461,7 +461,6 @@ struct PairCfgT {
     // fp32 chunks per warp in flight.  Two (proj: its epilogue is as long as
     // its K = 1024 mainloop, and exposed at one or two images) cost 32 KB,
     // paid for with a 5-deep ring; the long-K fc2 keeps one and 6 stages.
-    static constexpr int RBUF = RBUF_;
     static constexpr uint32_t kResidBuf = 32 * 32 * 4;
     __host__ __device__ static constexpr int stages(int EPI) {
         return EPI == kEpiResid && RBUF_ == 2 ? 5 : STAGES;
