@@ -69,3 +69,13 @@ def test_multi_gpu_handle_fails_cleanly_without_arguments(libs3t):
     assert b"devices" in libs3t.s3t_last_error()
     assert libs3t.s3t_multi_run(None, None, 1, None, 0, None) == -1
     assert libs3t.s3t_multi_num_devices(None) == 0
+
+
+def test_dropin_library_resolves_every_symbol(libs3t):
+    """The reference linked with the drop-in trunk (oracle/_ref/libsam3ref_s3t.so,
+    built by `make -C oracle dropin`) loads with every symbol resolved: the
+    harness's neck entries need the reference's own src/vision_neck.cpp."""
+    lib = ROOT / "oracle" / "_ref" / "libsam3ref_s3t.so"
+    if not lib.exists():
+        pytest.skip("drop-in reference library not built")
+    C.CDLL(str(lib), mode=C.RTLD_GLOBAL)
