@@ -700,6 +700,16 @@ int trunk_graph(s3t_ctx* c, const float* din, int batch, int n_layers, float* do
 // Images per pipelined chunk when both buffers are on the host.
 constexpr int kHostChunk = 8;
 
+// Images per pipelined chunk for a host-buffer batch: 8, or half the batch
+// for 5 to 16 images (the exposed first upload and last download of a whole
+// 8-image batch, 270 MB, cost more than running it as two 4-image chunks);
+// 0 when the batch runs as one piece.
+int host_chunk(int batch) {
+    if (batch > 2 * kHostChunk) return kHostChunk;
+    if (batch > 4) return (batch + 1) / 2;
+    return 0;
+}
+
 int ensure_events(s3t_ctx* c, size_t n) {
     while (c->events.size() < n) {
         cudaEvent_t e;
@@ -716,7 +726,8 @@ int ensure_events(s3t_ctx* c, size_t n) {
 // engines) while the trunk runs chunk k on `st`, so only the first upload
 // and the last download are not hidden behind compute.
 int run_host_pipelined(s3t_ctx* c, const float* images, int batch, int n_layers, float* out, cudaStream_t st) {
-    const int nc = (batch + kHostChunk - 1) / kHostChunk;
+    const int chunk = host_chunk(batch);
+    const int nc = (batch + chunk - 1) / chunk;
     if (ensure_events(c, size_t(2 * nc + 1))) return -1;
     const size_t img_elems = size_t(3) * kImage * kImage, out_elems = size_t(kDim) * kTokens;
     cudaEvent_t start = c->events[2 * nc];
@@ -724,13 +735,13 @@ int run_host_pipelined(s3t_ctx* c, const float* images, int batch, int n_layers,
     S3T_CUDA(cudaStreamWaitEvent(c->copy_in, start, 0));
     S3T_CUDA(cudaStreamWaitEvent(c->copy_out, start, 0));
     for (int k = 0; k < nc; ++k) {
-        const int b0 = k * kHostChunk, nb = std::min(kHostChunk, batch - b0);
+        const int b0 = k * chunk, nb = std::min(chunk, batch - b0);
         S3T_CUDA(cudaMemcpyAsync(c->img + b0 * img_elems, images + b0 * img_elems, nb * img_elems * 4,
                                  cudaMemcpyHostToDevice, c->copy_in));
         S3T_CUDA(cudaEventRecord(c->events[k], c->copy_in));
     }
     for (int k = 0; k < nc; ++k) {
-        const int b0 = k * kHostChunk, nb = std::min(kHostChunk, batch - b0);
+        const int b0 = k * chunk, nb = std::min(chunk, batch - b0);
         cudaGraphExec_t g = nullptr;
         if (trunk_graph(c, c->img + b0 * img_elems, nb, n_layers, c->out + b0 * out_elems, &g)) return -1;
         S3T_CUDA(cudaStreamWaitEvent(st, c->events[k], 0));
@@ -756,7 +767,7 @@ int run_impl(s3t_ctx* c, const float* images, int batch, int n_layers, float* ou
     if (ensure_workspace(c, batch)) return -1;
 
     const bool in_dev = flags & S3T_IMAGES_ON_DEVICE, out_dev = flags & S3T_OUTPUT_ON_DEVICE;
-    if (!in_dev && !out_dev && n_layers > 0 && batch > kHostChunk)
+    if (!in_dev && !out_dev && n_layers > 0 && host_chunk(batch) > 0)
         return run_host_pipelined(c, images, batch, n_layers, out, st);
 
     const size_t in_bytes = size_t(batch) * 3 * kImage * kImage * 4;
