@@ -457,8 +457,10 @@ def encoder_attention_extras(torch, dev, stream, s3t, images=4):
 
 
 def config_extras(torch, dev, stream, trunk, syn, s3t):
-    """Single-GPU extras: b=1 F16 p50 latency (device in -> device out),
-    Q8_0 batch-8 throughput and the bf16 attention microbenchmark."""
+    """Single-GPU extras: b=1 F16 p50 latency (device in -> device out, and
+    host in -> host out by wall clock: the host call returns once the features
+    are in host memory), Q8_0 batch-8 throughput and the bf16 attention
+    microbenchmark."""
     img = torch.from_numpy(syn.synthetic_images(1)).to(dev)
     out = torch.empty((1, 1024, 72, 72), device=dev)
     lat = []
@@ -472,6 +474,17 @@ def config_extras(torch, dev, stream, trunk, syn, s3t):
             lat.append(e0.elapsed_time(e1))
     res = {"latency_b1_p50_ms": round(statistics.median(lat), 3),
            "latency_b1_p90_ms": round(sorted(lat)[int(0.9 * len(lat))], 3)}
+    # the same from pinned host image to pinned host features (H2D 12.2 MB, D2H 21.2 MB)
+    img_h = img.cpu().pin_memory()
+    out_h = torch.empty((1, 1024, 72, 72)).pin_memory()
+    lat_h = []
+    for i in range(60):
+        t0 = time.perf_counter()
+        trunk.run_device(img_h.data_ptr(), 1, out_h.data_ptr(), stream.cuda_stream, images_on_device=False,
+                         output_on_device=False)
+        if i >= 10:
+            lat_h.append((time.perf_counter() - t0) * 1e3)
+    res["latency_b1_host_p50_ms"] = round(statistics.median(lat_h), 3)
     try:
         qm = s3t.GgufModel(syn.synthetic_gguf("q8_0"), device=dev.index)
         qt = s3t.VisionTrunk(qm)
