@@ -78,4 +78,6 @@ def test_dropin_library_resolves_every_symbol(libs3t):
     lib = ROOT / "oracle" / "_ref" / "libsam3ref_s3t.so"
     if not lib.exists():
         pytest.skip("drop-in reference library not built")
-    C.CDLL(str(lib), mode=C.RTLD_GLOBAL)
+    # RTLD_LOCAL: this library carries its own ggml build, which must not
+    # stand in for the symbols of the reference builds later tests load.
+    C.CDLL(str(lib), mode=C.RTLD_LOCAL)
