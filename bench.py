@@ -329,7 +329,9 @@ def _run_ours(a, torch, dist, world, rank, local, dev):
                 "h2d_bytes_per_step": int(imgs_host.numel() * 4 * world),
                 "d2h_bytes_per_step": int(out_host.numel() * 4 * world),
                 "wall_s": round(e2e_wall, 3)},
-        "clocks": clk.summary(),
+        "clocks": (clocks := clk.summary()),
+        # step time x median SM clock: comparable across runs whose power-capped clocks differ
+        "ms_per_step_x_sm_ghz": round(ms_step * clocks["sm_mhz"] / 1e3, 3) if clocks["sm_mhz"] else None,
         "gpu_launches": LAUNCHES_PER_TRUNK * len(chunks) * a.steps * world,
         **parts,
         **q8,
